@@ -1,0 +1,408 @@
+#!/usr/bin/env python
+"""Benchmark of the W4A8 MoE layer (grouped GEMM hot path) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload deepseek_ep] [--tokens T]
+
+One "step" is one routed MoE layer forward over one batch of synthetic tokens:
+align -> quantise+dispatch -> gate/up grouped GEMM -> SiLU-mul requant ->
+down grouped GEMM -> combine (and, for N > 1, the expert-parallel NCCL
+all-to-all dispatch and combine).  Default workload: the DeepSeek-V3-shaped
+layer (hidden 7168, moe intermediate 2048, 256 experts, top-8, group 128) at
+16384 tokens per GPU, i.e. the per-GPU shape of the expert-parallel
+configuration; at N = 1 all 256 experts are local.
+
+Prints ONE JSON line on rank 0.  `value` is whole-job tokens/s (device time,
+max over ranks), `e2e` the same through host buffers (pinned H2D of the
+step's tokens and routing, D2H of the output), `roofline` describes the
+dominant kernel (the gate/up grouped GEMM), `cpu_baseline` the reference
+algorithm restated on the CPU (oracle/, torch CPU, all host threads) timed on
+a bounded sample of the same workload.
+
+--impl reference times that CPU restatement alone (rank 0; other ranks exit 0).
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+PKG_NAME = "flagos-kernel-gen_b200"
+METRIC = "MoE layer tokens/s"
+
+
+def load_peaks() -> dict:
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return dict(hbm_gbs=float(d["hbm_gbs"]), bf16_tflops=float(d["bf16_tflops"]),
+                    bf16_tflops_sustained=float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), src="measured")
+    return dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0, src="fallback")
+
+
+def parse_workload(name: str, tokens: int | None):
+    W = importlib.import_module(PKG_NAME).workloads
+    m = re.fullmatch(r"([a-z0-9_]+?)(?:_T(\d+))?", name)
+    base, t = m.group(1), m.group(2)
+    ep = False
+    if base.endswith("_ep"):
+        base, ep = base[:-3], True
+    cfg = W.CONFIGS[base]
+    T = tokens or (int(t) if t else (16384 if ep else 8192))
+    return cfg, T
+
+
+def traffic_from_profiles(workload: str, kernel: str):
+    """Per-launch DRAM bytes of `kernel` on `workload` from the committed ncu
+    summaries (line format: `traffic_per_launch <workload> <kernel> <bytes>`)."""
+    d = os.path.join(REPO, "profiles")
+    if not os.path.isdir(d):
+        return None
+    for f in sorted(os.listdir(d)):
+        if not f.endswith((".md", ".txt")):
+            continue
+        for line in open(os.path.join(d, f), encoding="utf-8"):
+            parts = line.strip().strip("`").split()
+            if len(parts) == 4 and parts[0] == "traffic_per_launch" and parts[1] == workload and parts[2] == kernel:
+                return float(parts[3])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ["clocks.sm", "clocks.max.sm", "clocks_event_reasons.hw_slowdown",
+              "clocks_event_reasons.hw_thermal_slowdown", "clocks_event_reasons.sw_thermal_slowdown",
+              "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={','.join(self.FIELDS)}", "--format=csv,noheader,nounits",
+                 "-lms", "50", "-i", ident], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            return None
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            p = [x.strip() for x in line.split(",")]
+            if len(p) != 6:
+                continue
+            try:
+                sm.append(float(p[0]))
+                smax = max(smax, float(p[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, p[2:]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU legs (oracle)
+def cpu_sample_step(O, cfg, inp, off, experts, T):
+    """One CPU pass of the reference algorithm over the routed rows of `experts`
+    (full per-expert work: unpack, per-group fp32 einsum, scales, SiLU-mul
+    requant, down projection).  Returns (seconds, rows)."""
+    rows = 0
+    t0 = time.perf_counter()
+    for e in experts:
+        m0, m1 = int(off[e]), int(off[e + 1])
+        if m1 <= m0:
+            continue
+        rows += m1 - m0
+        xq, xs = inp["xq"][m0:m1], inp["xs"][m0:m1]
+        sub = torch.tensor([0, m1 - m0], dtype=torch.int32)
+        w13 = [t[e:e + 1] for t in inp["w13"]]
+        h = O.group_gemm(xq, xs, *w13, sub, torch.empty((m1 - m0, w13[0].shape[1]), dtype=torch.bfloat16),
+                         cfg.group_size)
+        if inp["w2"] is not None:
+            aq, as_ = O.silu_mul_requant(h)
+            w2 = [t[e:e + 1] for t in inp["w2"]]
+            O.group_gemm(torch.from_numpy(aq), torch.from_numpy(as_), *w2, sub,
+                         torch.empty((m1 - m0, w2[0].shape[1]), dtype=torch.bfloat16), cfg.group_size)
+    return time.perf_counter() - t0, rows
+
+
+def cpu_inputs(cfg, T, seed=0):
+    """CPU copies of the workload for the oracle legs: routing and quantised,
+    expert-sorted rows come from the CPU restatements; weights only for the
+    experts a sample touches are materialised (generated per expert)."""
+    from oracle import w4a8_oracle as O
+    W = importlib.import_module(PKG_NAME).workloads
+    inp = W.make_moe_inputs(cfg, T, seed=seed, weights=False)
+    al = O.moe_align(inp.topk_ids, cfg.experts, 128)
+    xq_tok, xs_tok = O.act_quant(inp.x)
+    src = al["sorted_ids"] // cfg.topk
+    return O, dict(xq=torch.from_numpy(xq_tok[src]), xs=torch.from_numpy(xs_tok[src])), al["expert_offsets"]
+
+
+def cpu_weights_for(cfg, experts, seed=1):
+    W = importlib.import_module(PKG_NAME).workloads
+    g = W.make_generator(seed)
+    n13 = 2 * cfg.inter if cfg.ffn else cfg.inter
+    w13 = [[], [], []]
+    w2 = [[], [], []]
+    for _ in experts:
+        for i, t in enumerate(W.make_int4_weights(1, n13, cfg.hidden, cfg.group_size, g)):
+            w13[i].append(t)
+        if cfg.ffn:
+            for i, t in enumerate(W.make_int4_weights(1, cfg.hidden, cfg.inter, cfg.group_size, g)):
+                w2[i].append(t)
+    cat = lambda L: [torch.cat(x, 0) for x in L]  # noqa: E731
+    return cat(w13), (cat(w2) if cfg.ffn else None)
+
+
+def run_cpu_leg(cfg, T, steps, warmup, budget_s):
+    """Times the CPU restatement: each step processes whole experts (the
+    busiest first) within a per-step time budget.  Returns the cpu_baseline dict."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    O, inp, off = cpu_inputs(cfg, T)
+    counts = off[1:] - off[:-1]
+    order = [int(e) for e in sorted(range(cfg.experts), key=lambda e: -int(counts[e])) if counts[e] > 0]
+    R = int(off[-1])
+    # calibrate with one expert
+    w13, w2 = cpu_weights_for(cfg, order[:1])
+    inp1 = dict(inp, w13=w13, w2=w2)
+    off1 = torch.tensor([0, int(counts[order[0]])], dtype=torch.int64)
+    inp1["xq"] = inp["xq"][int(off[order[0]]):int(off[order[0] + 1])]
+    inp1["xs"] = inp["xs"][int(off[order[0]]):int(off[order[0] + 1])]
+    t1, _ = cpu_sample_step(O, cfg, inp1, off1, [0], T)
+    n_exp = max(1, min(len(order), int(budget_s / max(t1, 1e-3))))
+    sample = order[:n_exp]
+    w13, w2 = cpu_weights_for(cfg, sample)
+    # re-index the sample's rows contiguously
+    xq = torch.cat([inp["xq"][int(off[e]):int(off[e + 1])] for e in sample])
+    xs = torch.cat([inp["xs"][int(off[e]):int(off[e + 1])] for e in sample])
+    c = torch.tensor([int(counts[e]) for e in sample])
+    soff = torch.cat([torch.zeros(1, dtype=torch.int64), torch.cumsum(c, 0)])
+    sinp = dict(xq=xq, xs=xs, w13=w13, w2=w2)
+    times, rows = [], 0
+    for i in range(warmup + steps):
+        dt, rows = cpu_sample_step(O, cfg, sinp, soff, list(range(len(sample))), T)
+        if i >= warmup:
+            times.append(dt)
+    t = statistics.median(times)
+    tok_s = T * (rows / R) / t
+    return {"value": tok_s, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{len(sample)} of {int((counts > 0).sum())} active experts ({rows} of {R} routed rows, "
+                      f"busiest first), full gate/up + SiLU-mul requant + down per expert, median of {steps} "
+                      f"step(s); tokens/s scaled by routed rows",
+            "seconds_per_step": t}
+
+
+# ----------------------------------------------------------------------------- GPU leg
+def build_layer(pkg, cfg, T, rank, world, dev):
+    W = pkg.workloads
+    gen = W.make_generator(1000 + rank, dev)
+    if world == 1:
+        n13 = 2 * cfg.inter if cfg.ffn else cfg.inter
+        w13 = pkg.W4A8Weights(*W.make_int4_weights(cfg.experts, n13, cfg.hidden, cfg.group_size, gen, dev))
+        w2 = pkg.W4A8Weights(*W.make_int4_weights(cfg.experts, cfg.hidden, cfg.inter, cfg.group_size, gen, dev)) \
+            if cfg.ffn else None
+        return pkg.MoELayer(w13, w2, cfg.group_size, cfg.topk, T)
+    ep = importlib.import_module(PKG_NAME + ".ep")
+    return ep.ExpertParallelMoE.with_synthetic_weights(cfg, T, rank, world, dev, gen)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="deepseek_ep")
+    ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=6.0, help="seconds of CPU work per baseline step")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg, T = parse_workload(args.workload, args.tokens)
+    config = {"workload": args.workload, "tokens_per_gpu": T, "hidden": cfg.hidden, "moe_inter": cfg.inter,
+              "experts": cfg.experts, "topk": cfg.topk, "group_size": cfg.group_size,
+              "routing": f"{cfg.scoring}" + (f"+zipf{cfg.zipf}" if cfg.zipf else " uniform"),
+              "parallelism": f"ep{world}" if world > 1 else "single", "l2": "inputs larger than L2 "
+              "(expert weights are GBs; no flush needed)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        steps = max(1, min(args.steps, 5))
+        warm = min(args.warmup, 1)
+        cb = run_cpu_leg(cfg, T, steps, warm, budget_s=args.cpu_budget)
+        line = {"metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": steps,
+                "warmup": warm, "ms_per_step": 1e3 * T / cb["value"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int4 -> int32/fp32 -> bf16",
+                "data": "synthetic (seeded; BASELINE.json distributions)", "config": config, "impl": "reference",
+                "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "note": "reference algorithm (docs/Task1.md:53-114 + FFN glue) restated in oracle/, torch CPU; "
+                        "the reference tree itself is Python and is not present on the GPU box"}
+        print(json.dumps(line), flush=True)
+        return
+
+    pkg = importlib.import_module(PKG_NAME)
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    W = pkg.workloads
+    layer = build_layer(pkg, cfg, T, rank, world, dev)
+    inp = W.make_moe_inputs(cfg, T, seed=7 + rank, device=dev, weights=False)
+    x, ids, tw = inp.x, inp.topk_ids, inp.topk_weights
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        layer(x, ids, tw)
+    barrier()
+    if pkg.device_status() != 0:
+        raise RuntimeError("device status error after warm-up")
+
+    # ---- device-timed steps (inputs resident in HBM)
+    sampler = ClockSampler(local_rank)
+    time.sleep(0.2)
+    events = []
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        layer(x, ids, tw, events=events)
+    t1.record()
+    barrier()
+    clocks = sampler.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    per_kernel = {}
+    for name, s, e in events:
+        per_kernel.setdefault(name, []).append(s.elapsed_time(e))
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        ms = float(tt.item())
+
+    # ---- end to end through the public API with host buffers
+    x_h = x.cpu().pin_memory()
+    ids_h = ids.cpu().pin_memory()
+    tw_h = tw.cpu().pin_memory()
+    out_h = torch.empty((T, layer.out.shape[1]), dtype=torch.bfloat16).pin_memory()
+    xd, idsd, twd = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(tw)
+
+    def e2e_step():
+        xd.copy_(x_h, non_blocking=True)
+        idsd.copy_(ids_h, non_blocking=True)
+        twd.copy_(tw_h, non_blocking=True)
+        o = layer(xd, idsd, twd)
+        out_h.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    h2d = x.numel() * 2 + ids.numel() * 4 + tw.numel() * 4
+    d2h = out_h.numel() * 2
+    status = pkg.device_status()
+
+    # ---- roofline of the dominant kernel (gate/up grouped GEMM)
+    peaks = load_peaks()
+    off = layer.offsets.cpu() if world == 1 else layer.local.offsets.cpu()
+    counts = (off[1:] - off[:-1])
+    active = int((counts > 0).sum())
+    R = int(off[-1])
+    n13 = 2 * cfg.inter if cfg.ffn else cfg.inter
+    gu_bytes = W.gemm_roofline_bytes(active, R, n13, cfg.hidden, cfg.group_size)
+    gu_ops = W.gemm_ops(R, n13, cfg.hidden)
+    gu_ms = statistics.mean(per_kernel["gemm_gate_up"])
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    t_hbm = gu_bytes / (peaks["hbm_gbs"] * 1e9)
+    t_tc = gu_ops / (int8_peak * 1e12)
+    if t_tc >= t_hbm:
+        achieved = gu_ops / (gu_ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
+                "frac": achieved / int8_peak}
+    else:
+        achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"]}
+    roof.update({"kernel": "w4a8 grouped GEMM (gate/up), gemm_tc_kernel", "ms_per_launch": gu_ms,
+                 "algorithmic_bytes": gu_bytes, "algorithmic_ops": gu_ops,
+                 "hbm_frac": gu_bytes / (gu_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                 "int8_frac": gu_ops / (gu_ms * 1e-3) / 1e12 / int8_peak,
+                 "traffic": traffic_from_profiles(args.workload, "gemm_tc_kernel"),
+                 "peak_source": f"{peaks['src']}: HBM = hbm_gbs; int8 = 2 x bf16_tflops (dense int8 rate is "
+                                f"twice bf16 on sm_100)"})
+    if "gemm_down" in per_kernel:
+        dn_ms = statistics.mean(per_kernel["gemm_down"])
+        roof["down_ms_per_launch"] = dn_ms
+        roof["down_int8_frac"] = W.gemm_ops(R, cfg.hidden, cfg.inter) / (dn_ms * 1e-3) / 1e12 / int8_peak
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cb = run_cpu_leg(cfg, T, steps=1, warmup=0, budget_s=args.cpu_budget)
+        cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": world * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int4 -> int32/fp32 -> bf16",
+                "data": "synthetic (seeded; BASELINE.json distributions; random-init weights)",
+                "config": config,
+                "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                "gpu_launches": args.steps * layer.launches_per_forward(),
+                "roofline": roof, "cpu_baseline": cpu, "clocks": clocks, "device_status": status,
+                "active_experts": active, "routed_rows": R}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

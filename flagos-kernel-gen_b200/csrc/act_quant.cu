@@ -1,0 +1,121 @@
+// Per-token symmetric int8 activation quantisation, and its fused variant that
+// writes each quantised token row straight to its top-k slots in expert-sorted
+// order (the dispatch step of the routed MoE layer).
+//
+// Convention (the repository's only int8 quantiser, docs/Task3.md:58-67):
+//   scale = max(amax / 127, 1e-10)         (IEEE fp32 division)
+//   q     = int8(trunc(clamp(x / scale, -127, 127)))   (.to(int8) truncates)
+// Every step is an exactly rounded fp32 operation, so the result is bit-exact
+// against any IEEE restatement of the same formula.
+#include "common.cuh"
+#include "w4a8_internal.h"
+
+namespace w4a8 {
+
+namespace {
+
+constexpr int kQThreads = 256;
+constexpr int kQMaxVec = 8;  // 8 x 8 bf16 per thread -> H <= 16384 on the register path
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, d));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = (l < (int)(blockDim.x >> 5)) ? red[l] : 0.f;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, d));
+    if (l == 0) red[0] = v;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+__device__ __forceinline__ int8_t quant1(float x, float s) {
+  float q = __fdiv_rn(x, s);
+  q = fminf(fmaxf(q, -127.f), 127.f);
+  return static_cast<int8_t>(__float2int_rz(q));
+}
+
+// One CTA per token row.  rows_out: nullptr -> write row t to out row t;
+// otherwise write row t to rows_out[t*topk + j] for j in [0, topk).
+__global__ void __launch_bounds__(kQThreads)
+act_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride0, int H,
+                 int8_t* __restrict__ q_out, int64_t q_stride0, float* __restrict__ s_out,
+                 const int32_t* __restrict__ rows_out, int topk) {
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  const __nv_bfloat16* xr = x + static_cast<int64_t>(t) * x_stride0;
+  const bool vec = ((H & 7) == 0) && ((reinterpret_cast<uintptr_t>(xr) & 15) == 0) &&
+                   (H / 8 <= kQThreads * kQMaxVec);
+  float amax = 0.f;
+  uint4 buf[kQMaxVec];
+  const int nv = H / 8;
+  if (vec) {
+#pragma unroll
+    for (int i = 0; i < kQMaxVec; ++i) {
+      const int v = threadIdx.x + i * kQThreads;
+      if (v < nv) {
+        buf[i] = __ldg(reinterpret_cast<const uint4*>(xr) + v);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&buf[i]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(h2[j]);
+          amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+      }
+    }
+  } else {
+    for (int k = threadIdx.x; k < H; k += kQThreads) amax = fmaxf(amax, fabsf(__bfloat162float(xr[k])));
+  }
+  amax = block_max(amax, red);
+  const float s = fmaxf(__fdiv_rn(amax, 127.f), 1e-10f);
+  const int ndst = rows_out ? topk : 1;
+  if (threadIdx.x < ndst) {
+    const int64_t row = rows_out ? rows_out[static_cast<int64_t>(t) * topk + threadIdx.x] : t;
+    if (row >= 0) s_out[row] = s;
+  }
+  for (int d = 0; d < ndst; ++d) {
+    const int64_t row = rows_out ? rows_out[static_cast<int64_t>(t) * topk + d] : t;
+    if (row < 0) continue;  // slot routed to no local expert
+    int8_t* qr = q_out + row * q_stride0;
+    if (vec && ((reinterpret_cast<uintptr_t>(qr) & 7) == 0)) {
+#pragma unroll
+      for (int i = 0; i < kQMaxVec; ++i) {
+        const int v = threadIdx.x + i * kQThreads;
+        if (v < nv) {
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&buf[i]);
+          uint32_t w[2];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const float2 f0 = __bfloat1622float2(h2[2 * j]);
+            const float2 f1 = __bfloat1622float2(h2[2 * j + 1]);
+            const uint32_t b0 = static_cast<uint8_t>(quant1(f0.x, s));
+            const uint32_t b1 = static_cast<uint8_t>(quant1(f0.y, s));
+            const uint32_t b2 = static_cast<uint8_t>(quant1(f1.x, s));
+            const uint32_t b3 = static_cast<uint8_t>(quant1(f1.y, s));
+            w[j] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+          }
+          reinterpret_cast<uint2*>(qr)[v] = make_uint2(w[0], w[1]);
+        }
+      }
+    } else {
+      for (int k = threadIdx.x; k < H; k += kQThreads) qr[k] = quant1(__bfloat162float(xr[k]), s);
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_act_quant(const __nv_bfloat16* x, int64_t x_stride0, int T, int H, int8_t* q,
+                             int64_t q_stride0, float* s, const int32_t* rows_out, int topk,
+                             cudaStream_t stream) {
+  if (T <= 0) return cudaSuccess;
+  act_quant_kernel<<<T, kQThreads, 0, stream>>>(x, x_stride0, H, q, q_stride0, s, rows_out, topk);
+  return cudaGetLastError();
+}
+
+}  // namespace w4a8

@@ -1,0 +1,261 @@
+// extern "C" entry points (include/w4a8moe.h): argument validation, device
+// status handling and kernel dispatch.  Validation mirrors the reference's
+// asserts (docs/Task1.md:74-75: K_half*2 == K, K % group_size == 0) and its
+// group-size rule (Task1/各平台最高/task1-海光-26.44.py:226: 64 or 128).
+#include "../../include/w4a8moe.h"
+#include "common.cuh"
+#include "w4a8_internal.h"
+
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+namespace w4a8 {
+cudaError_t launch_act_quant(const __nv_bfloat16* x, int64_t x_stride0, int T, int H, int8_t* q,
+                             int64_t q_stride0, float* s, const int32_t* rows_out, int topk,
+                             cudaStream_t stream);
+size_t align_workspace_bytes(int R, int E);
+cudaError_t launch_moe_align(const int32_t* ids, int R, int E, int bs, int32_t* expert_offsets,
+                             int32_t* sorted_ids, int32_t* inv_pos, int32_t* padded_ids,
+                             int32_t* block_expert, int32_t* num_post_pad, void* workspace,
+                             cudaStream_t stream);
+cudaError_t launch_silu_mul_requant(const __nv_bfloat16* h, int64_t h_stride0, int R, int I, int8_t* q,
+                                    int64_t q_stride0, float* s, const int32_t* valid_rows,
+                                    cudaStream_t stream);
+cudaError_t launch_moe_combine(const __nv_bfloat16* y, int64_t y_stride0, const int32_t* inv_pos,
+                               const float* topk_w, int T, int topk, int H, __nv_bfloat16* out,
+                               int64_t out_stride0, cudaStream_t stream);
+
+namespace {
+__device__ int g_status_word;
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(W4A8_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+constexpr int kMaxDevices = 64;
+int* g_status_ptr[kMaxDevices] = {};
+std::mutex g_status_mu;
+// Makes the stream's device current in this library's runtime.  The library
+// links its own (static) CUDA runtime, whose notion of the "current device"
+// is separate from the caller's; the stream is the authoritative handle.
+cudaError_t bind_stream_device(void* stream) {
+  if (stream == nullptr) return cudaSuccess;
+  int sdev = 0, cur = 0;
+  cudaError_t e = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev);
+  if (e != cudaSuccess) return e;
+  e = cudaGetDevice(&cur);
+  if (e != cudaSuccess) return e;
+  return sdev == cur ? cudaSuccess : cudaSetDevice(sdev);
+}
+}  // namespace
+
+int* device_status_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lk(g_status_mu);
+  if (g_status_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
+    g_status_ptr[dev] = static_cast<int*>(p);
+  }
+  return g_status_ptr[dev];
+}
+
+}  // namespace w4a8
+
+using namespace w4a8;
+
+extern "C" {
+
+int w4a8_abi_version(void) { return 1; }
+
+const char* w4a8_last_error(void) { return g_last_error.c_str(); }
+
+int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
+                           const uint8_t* w_q4_packed, const float* w_scale, const int8_t* w_zero,
+                           const int32_t* expert_offsets, void* out, int64_t out_stride0,
+                           int64_t out_stride1, int64_t M_total, int64_t E, int64_t N, int64_t K,
+                           int64_t group_size, int32_t kernel, int32_t* partials, void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+  if (group_size != 64 && group_size != 128)
+    return fail(W4A8_ERR_INVALID, "group_size must be 64 or 128 (got %lld)", (long long)group_size);
+  if (K <= 0 || K % group_size != 0)
+    return fail(W4A8_ERR_INVALID, "K %% group_size != 0 (K=%lld, group_size=%lld)", (long long)K,
+                (long long)group_size);
+  if (M_total < 0 || E <= 0 || N <= 0)
+    return fail(W4A8_ERR_INVALID, "bad sizes M_total=%lld E=%lld N=%lld", (long long)M_total, (long long)E,
+                (long long)N);
+  if (M_total > INT32_MAX || E * N > INT32_MAX || K > INT32_MAX || E > 4096)
+    return fail(W4A8_ERR_INVALID, "sizes exceed the 32-bit index range of the kernels");
+  if (M_total > 0 && (x_q == nullptr || x_scale == nullptr || out == nullptr))
+    return fail(W4A8_ERR_INVALID, "null activation / output pointer");
+  if (w_q4_packed == nullptr || w_scale == nullptr || w_zero == nullptr || expert_offsets == nullptr)
+    return fail(W4A8_ERR_INVALID, "null weight / offset pointer");
+  if (x_stride0 < K) return fail(W4A8_ERR_INVALID, "x_q row stride %lld < K", (long long)x_stride0);
+  if (kernel != W4A8_KERNEL_AUTO && kernel != W4A8_KERNEL_TC && kernel != W4A8_KERNEL_SIMT)
+    return fail(W4A8_ERR_INVALID, "unknown kernel selector %d", kernel);
+  if (M_total == 0) return W4A8_OK;
+
+  GemmArgs a{};
+  a.x_q = x_q;
+  a.x_scale = x_scale;
+  a.w_packed = w_q4_packed;
+  a.w_scale = w_scale;
+  a.w_zero = w_zero;
+  a.offsets = expert_offsets;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.partials = partials;
+  a.status = device_status_ptr();
+  if (a.status == nullptr) return fail(W4A8_ERR_CUDA, "cannot resolve the device status word");
+  a.x_stride0 = x_stride0;
+  a.out_stride0 = out_stride0;
+  a.out_stride1 = out_stride1;
+  a.M_total = static_cast<int>(M_total);
+  a.E = static_cast<int>(E);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.gs = static_cast<int>(group_size);
+
+  const bool tc_ok = K >= 128 && (reinterpret_cast<uintptr_t>(x_q) % 16 == 0) && (x_stride0 % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(w_q4_packed) % 16 == 0);
+  const bool simt_ok = (reinterpret_cast<uintptr_t>(x_q) % 4 == 0) && (x_stride0 % 4 == 0);
+  int use = kernel;
+  if (use == W4A8_KERNEL_AUTO) use = tc_ok ? W4A8_KERNEL_TC : W4A8_KERNEL_SIMT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (use == W4A8_KERNEL_TC) {
+    if (!tc_ok)
+      return fail(W4A8_ERR_INVALID,
+                  "tensor-core kernel needs K >= 128 and 16-byte aligned x_q rows / weights");
+    e = launch_gemm_tc(a, st);
+  } else if (use == W4A8_KERNEL_SIMT) {
+    if (!simt_ok) return fail(W4A8_ERR_INVALID, "CUDA-core kernel needs 4-byte aligned x_q rows");
+    e = launch_gemm_simt(a, st);
+  } else {
+    return fail(W4A8_ERR_INVALID, "unknown kernel selector %d", kernel);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "grouped GEMM launch");
+  return W4A8_OK;
+}
+
+int w4a8_group_gemm_moe(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
+                        const uint8_t* w_q4_packed, const float* w_scale, const int8_t* w_zero,
+                        const int32_t* expert_offsets, void* out, int64_t out_stride0,
+                        int64_t out_stride1, int64_t M_total, int64_t E, int64_t N, int64_t K,
+                        int64_t group_size, void* stream) {
+  return w4a8_group_gemm_moe_ex(x_q, x_stride0, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, out,
+                                out_stride0, out_stride1, M_total, E, N, K, group_size, W4A8_KERNEL_AUTO,
+                                nullptr, stream);
+}
+
+int w4a8_act_quant(const void* x, int64_t x_stride0, int64_t T, int64_t H, int8_t* x_q, int64_t q_stride0,
+                   float* x_scale, void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+  if (T < 0 || H <= 0 || T > INT32_MAX || H > INT32_MAX)
+    return fail(W4A8_ERR_INVALID, "bad sizes T=%lld H=%lld", (long long)T, (long long)H);
+  if (T == 0) return W4A8_OK;
+  if (x == nullptr || x_q == nullptr || x_scale == nullptr) return fail(W4A8_ERR_INVALID, "null pointer");
+  cudaError_t e = launch_act_quant(static_cast<const __nv_bfloat16*>(x), x_stride0, (int)T, (int)H, x_q,
+                                   q_stride0, x_scale, nullptr, 1, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? W4A8_OK : cuda_fail(e, "act_quant launch");
+}
+
+int w4a8_quant_scatter(const void* x, int64_t x_stride0, int64_t T, int64_t H, const int32_t* inv_pos,
+                       int64_t topk, int8_t* x_sorted, float* xs_sorted, void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+  if (T < 0 || H <= 0 || topk <= 0 || topk > 256 || T * topk > INT32_MAX || H > INT32_MAX)
+    return fail(W4A8_ERR_INVALID, "bad sizes T=%lld H=%lld topk=%lld", (long long)T, (long long)H,
+                (long long)topk);
+  if (T == 0) return W4A8_OK;
+  if (x == nullptr || inv_pos == nullptr || x_sorted == nullptr || xs_sorted == nullptr)
+    return fail(W4A8_ERR_INVALID, "null pointer");
+  cudaError_t e = launch_act_quant(static_cast<const __nv_bfloat16*>(x), x_stride0, (int)T, (int)H, x_sorted,
+                                   H, xs_sorted, inv_pos, (int)topk, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? W4A8_OK : cuda_fail(e, "quant_scatter launch");
+}
+
+size_t w4a8_moe_align_workspace_size(int64_t T, int64_t topk, int64_t E) {
+  if (T < 0 || topk <= 0 || E <= 0 || T * topk > INT32_MAX) return 0;
+  return align_workspace_bytes((int)(T * topk), (int)E);
+}
+
+int w4a8_moe_align(const int32_t* topk_ids, int64_t T, int64_t topk, int64_t E, int64_t block_size,
+                   int32_t* expert_offsets, int32_t* sorted_ids, int32_t* inv_pos, int32_t* padded_ids,
+                   int32_t* block_expert, int32_t* num_post_pad, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+  if (T < 0 || topk <= 0 || E <= 0 || E > 8192 || block_size <= 0 || T * topk > INT32_MAX / 2)
+    return fail(W4A8_ERR_INVALID, "bad sizes T=%lld topk=%lld E=%lld block_size=%lld", (long long)T,
+                (long long)topk, (long long)E, (long long)block_size);
+  if (expert_offsets == nullptr || (T > 0 && (topk_ids == nullptr || sorted_ids == nullptr || inv_pos == nullptr)))
+    return fail(W4A8_ERR_INVALID, "null pointer");
+  const size_t need = w4a8_moe_align_workspace_size(T, topk, E);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(W4A8_ERR_INVALID, "workspace too small (%zu < %zu bytes)", workspace_bytes, need);
+  cudaError_t e = launch_moe_align(topk_ids, (int)(T * topk), (int)E, (int)block_size, expert_offsets,
+                                   sorted_ids, inv_pos, padded_ids, block_expert, num_post_pad, workspace,
+                                   static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? W4A8_OK : cuda_fail(e, "moe_align launch");
+}
+
+int w4a8_silu_mul_requant(const void* h, int64_t h_stride0, int64_t R, int64_t I, int8_t* q, float* s,
+                          void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+  if (R < 0 || I <= 0 || I > 16384 || R > INT32_MAX || h_stride0 < 2 * I)
+    return fail(W4A8_ERR_INVALID, "bad sizes R=%lld I=%lld (I <= 16384)", (long long)R, (long long)I);
+  if (R == 0) return W4A8_OK;
+  if (h == nullptr || q == nullptr || s == nullptr) return fail(W4A8_ERR_INVALID, "null pointer");
+  cudaError_t e = launch_silu_mul_requant(static_cast<const __nv_bfloat16*>(h), h_stride0, (int)R, (int)I, q, I,
+                                          s, nullptr, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? W4A8_OK : cuda_fail(e, "silu_mul_requant launch");
+}
+
+int w4a8_moe_combine(const void* y, int64_t y_stride0, const int32_t* inv_pos, const float* topk_w, int64_t T,
+                     int64_t topk, int64_t H, void* out, int64_t out_stride0, void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+  if (T < 0 || topk <= 0 || H <= 0 || T > INT32_MAX || H > INT32_MAX)
+    return fail(W4A8_ERR_INVALID, "bad sizes T=%lld topk=%lld H=%lld", (long long)T, (long long)topk,
+                (long long)H);
+  if (T == 0) return W4A8_OK;
+  if (y == nullptr || inv_pos == nullptr || topk_w == nullptr || out == nullptr)
+    return fail(W4A8_ERR_INVALID, "null pointer");
+  cudaError_t e = launch_moe_combine(static_cast<const __nv_bfloat16*>(y), y_stride0, inv_pos, topk_w, (int)T,
+                                     (int)topk, (int)H, static_cast<__nv_bfloat16*>(out), out_stride0,
+                                     static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? W4A8_OK : cuda_fail(e, "moe_combine launch");
+}
+
+int w4a8_device_status(int32_t* status_out, int32_t reset, void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+  int* p = device_status_ptr();
+  if (p == nullptr) return fail(W4A8_ERR_CUDA, "cannot resolve the device status word");
+  int v = 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(&v, p, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "device status read");
+  if (reset && v != 0) {
+    e = cudaMemsetAsync(p, 0, sizeof(int), st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "device status reset");
+  }
+  if (status_out) *status_out = v;
+  return W4A8_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,154 @@
+// Routed-MoE glue kernels around the grouped GEMM.
+//
+// silu_mul_requant: h bf16 [R, 2I] (gate = h[:, :I], up = h[:, I:], the split
+//   of docs/Task3.md:99-100) -> y = silu(gate) * up in fp32 (forward formula of
+//   docs/Task3.md:107-110) -> per-row symmetric int8 with the quantiser of
+//   docs/Task3.md:58-67 (scale = max(amax/127, 1e-10), truncating cast).
+// moe_combine: out[t, :] = bf16( sum_{j ascending} topk_w[t, j] * y[inv_pos[t*k+j], :] )
+//   with each product and each sum rounded to fp32 (no FMA contraction), so
+//   the result is bit-exact against the same loop on the CPU.
+#include "common.cuh"
+#include "w4a8_internal.h"
+
+namespace w4a8 {
+
+namespace {
+
+constexpr int kGThreads = 256;
+
+__device__ __forceinline__ float block_max256(float v, float* red) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, d));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = (l < kGThreads / 32) ? red[l] : 0.f;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, d));
+    if (l == 0) red[0] = v;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  const float sig = 1.0f / (1.0f + expf(-g));
+  return __fmul_rn(__fmul_rn(g, sig), u);
+}
+
+// One CTA per row.  The fp32 products are staged in shared memory (I <= 16384).
+__global__ void __launch_bounds__(kGThreads)
+silu_mul_requant_kernel(const __nv_bfloat16* __restrict__ h, int64_t h_stride0, int I,
+                        int8_t* __restrict__ q, int64_t q_stride0, float* __restrict__ s_out,
+                        const int32_t* __restrict__ valid_rows) {
+  extern __shared__ float s_y[];
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  if (valid_rows != nullptr && row >= *valid_rows) return;
+  const __nv_bfloat16* hr = h + row * h_stride0;
+  float amax = 0.f;
+  const bool vec = ((I & 1) == 0) && ((reinterpret_cast<uintptr_t>(hr) & 3) == 0);
+  if (vec) {
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(hr);
+    const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(hr + I);
+    for (int i = threadIdx.x; i < I / 2; i += kGThreads) {
+      const float2 g = __bfloat1622float2(g2[i]);
+      const float2 u = __bfloat1622float2(u2[i]);
+      const float y0 = silu_mul(g.x, u.x), y1 = silu_mul(g.y, u.y);
+      s_y[2 * i] = y0;
+      s_y[2 * i + 1] = y1;
+      amax = fmaxf(amax, fmaxf(fabsf(y0), fabsf(y1)));
+    }
+  } else {
+    for (int i = threadIdx.x; i < I; i += kGThreads) {
+      const float y = silu_mul(__bfloat162float(hr[i]), __bfloat162float(hr[I + i]));
+      s_y[i] = y;
+      amax = fmaxf(amax, fabsf(y));
+    }
+  }
+  amax = block_max256(amax, red);
+  const float s = fmaxf(__fdiv_rn(amax, 127.f), 1e-10f);
+  if (threadIdx.x == 0) s_out[row] = s;
+  int8_t* qr = q + row * q_stride0;
+  for (int i = threadIdx.x; i < I; i += kGThreads) {
+    float v = __fdiv_rn(s_y[i], s);
+    v = fminf(fmaxf(v, -127.f), 127.f);
+    qr[i] = static_cast<int8_t>(__float2int_rz(v));
+  }
+}
+
+// One CTA per token; each thread owns 8 consecutive columns (16-byte vectors).
+__global__ void __launch_bounds__(kGThreads)
+moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int64_t y_stride0, const int32_t* __restrict__ inv_pos,
+                   const float* __restrict__ topk_w, int topk, int H, __nv_bfloat16* __restrict__ out,
+                   int64_t out_stride0) {
+  const int t = blockIdx.x;
+  const int32_t* pos = inv_pos + static_cast<int64_t>(t) * topk;
+  const float* wt = topk_w + static_cast<int64_t>(t) * topk;
+  __nv_bfloat16* o = out + static_cast<int64_t>(t) * out_stride0;
+  const bool vec = ((H & 7) == 0) && ((y_stride0 & 7) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0) &&
+                   ((reinterpret_cast<uintptr_t>(o) & 15) == 0);
+  if (vec) {
+    for (int c = threadIdx.x; c < H / 8; c += kGThreads) {
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+      for (int j = 0; j < topk; ++j) {
+        const int p = pos[j];
+        if (p < 0) continue;
+        const float w = wt[j];
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(p) * y_stride0) + c);
+        const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(v2[i]);
+          acc[2 * i] = __fadd_rn(acc[2 * i], __fmul_rn(w, f.x));
+          acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __fmul_rn(w, f.y));
+        }
+      }
+      uint4 r;
+      __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) r2[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+      reinterpret_cast<uint4*>(o)[c] = r;
+    }
+  } else {
+    for (int c = threadIdx.x; c < H; c += kGThreads) {
+      float acc = 0.f;
+      for (int j = 0; j < topk; ++j) {
+        const int p = pos[j];
+        if (p < 0) continue;
+        acc = __fadd_rn(acc, __fmul_rn(wt[j], __bfloat162float(y[static_cast<int64_t>(p) * y_stride0 + c])));
+      }
+      o[c] = __float2bfloat16_rn(acc);
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_silu_mul_requant(const __nv_bfloat16* h, int64_t h_stride0, int R, int I, int8_t* q,
+                                    int64_t q_stride0, float* s, const int32_t* valid_rows,
+                                    cudaStream_t stream) {
+  if (R <= 0) return cudaSuccess;
+  const size_t smem = sizeof(float) * static_cast<size_t>(I);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(silu_mul_requant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  silu_mul_requant_kernel<<<R, kGThreads, smem, stream>>>(h, h_stride0, I, q, q_stride0, s, valid_rows);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_moe_combine(const __nv_bfloat16* y, int64_t y_stride0, const int32_t* inv_pos,
+                               const float* topk_w, int T, int topk, int H, __nv_bfloat16* out,
+                               int64_t out_stride0, cudaStream_t stream) {
+  if (T <= 0) return cudaSuccess;
+  moe_combine_kernel<<<T, kGThreads, 0, stream>>>(y, y_stride0, inv_pos, topk_w, topk, H, out, out_stride0);
+  return cudaGetLastError();
+}
+
+}  // namespace w4a8

@@ -1,0 +1,162 @@
+"""Routed W4A8 MoE layer built on the reference operator.
+
+The reference has only the grouped GEMM over pre-grouped rows
+(docs/Task1.md:8-17).  A routed layer adds the stages around it; every stage
+is one CUDA kernel of this library, and nothing synchronises the host:
+
+  1. moe_align        topk_ids [T, k] -> expert_offsets, sorted order, inverse
+  2. quant_scatter    x bf16 [T, H] -> int8 rows in expert-sorted order + scales
+  3. grouped GEMM     gate/up:  [R, H] x W13[E, 2I, H] -> h bf16 [R, 2I]
+  4. silu_mul_requant h -> int8 [R, I] + per-row scale
+  5. grouped GEMM     down:     [R, I] x W2[E, H, I] -> y bf16 [R, H]
+  6. moe_combine      out[t] = bf16(sum_j w[t, j] * y[pos(t, j)])
+
+(R = T * k.)  For the single-GEMM form (no down projection) steps 4-5 are
+skipped and the combine runs on the gate/up output.
+
+``MoELayer`` keeps all intermediates in preallocated buffers sized for a
+maximum token count, so a step allocates nothing and can be replayed from a
+CUDA graph.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from . import ops
+
+
+@dataclass
+class W4A8Weights:
+    """One projection: packed int4 [E, N, K/2] + scale / zero [E, N, K/gs]."""
+    packed: torch.Tensor
+    scale: torch.Tensor
+    zero: torch.Tensor
+
+    @property
+    def shape(self):
+        E, N, Kh = self.packed.shape
+        return E, N, 2 * Kh
+
+
+class _Ev:
+    """Optional CUDA-event bracketing of a stage (no-op when events is None)."""
+
+    def __init__(self, events):
+        self.events = events
+        self.cur = None
+
+    def start(self, name):
+        if self.events is not None:
+            s = torch.cuda.Event(enable_timing=True)
+            s.record()
+            self.cur = (name, s)
+
+    def stop(self):
+        if self.events is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.events.append((self.cur[0], self.cur[1], e))
+
+
+class MoELayer:
+    """Routed W4A8 MoE (gate/up -> SiLU-mul -> down, or a single up GEMM)."""
+
+    def __init__(self, w13: W4A8Weights, w2: W4A8Weights | None, group_size: int, topk: int,
+                 max_tokens: int, align_block: int = 128):
+        self.w13, self.w2 = w13, w2
+        self.gs, self.topk = group_size, topk
+        E, N13, H = w13.shape
+        self.E, self.H = E, H
+        self.ffn = w2 is not None
+        self.I = N13 // 2 if self.ffn else N13
+        if self.ffn:
+            E2, H2, I2 = w2.shape
+            if E2 != E or H2 != H or I2 != self.I:
+                raise ValueError("w2 must be [E, H, I] for w13 [E, 2I, H]")
+        self.align_block = align_block
+        self.device = w13.packed.device
+        self._alloc(max_tokens)
+
+    def _alloc(self, max_tokens: int):
+        dev, E, H, I, k = self.device, self.E, self.H, self.I, self.topk
+        self.max_tokens = max_tokens
+        R = max_tokens * k
+        cap, nblk = ops.align_capacity(R, E, self.align_block)
+        lib = _lib.load()
+        ws_bytes = max(int(lib.w4a8_moe_align_workspace_size(max_tokens, k, E)), 4)
+        self.ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.offsets = torch.empty((E + 1,), **i32)
+        self.sorted_ids = torch.empty((R,), **i32)
+        self.inv_pos = torch.empty((R,), **i32)
+        self.padded_ids = torch.empty((cap,), **i32)
+        self.block_expert = torch.empty((nblk,), **i32)
+        self.num_post_pad = torch.empty((1,), **i32)
+        self.xq = torch.empty((R, H), dtype=torch.int8, device=dev)
+        self.xs = torch.empty((R,), dtype=torch.float32, device=dev)
+        n13 = 2 * I if self.ffn else I
+        self.h = torch.empty((R, n13), dtype=torch.bfloat16, device=dev)
+        if self.ffn:
+            self.aq = torch.empty((R, I), dtype=torch.int8, device=dev)
+            self.as_ = torch.empty((R,), dtype=torch.float32, device=dev)
+            self.y = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
+        self.out = torch.empty((max_tokens, H if self.ffn else I), dtype=torch.bfloat16, device=dev)
+
+    # number of library kernel launches per forward (for launch accounting)
+    def launches_per_forward(self) -> int:
+        # align: 3, quant_scatter: 1, gemm: 1 (+1), silu: (1), combine: 1
+        return 3 + 1 + 1 + (2 if self.ffn else 0) + 1
+
+    def forward(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+                out: torch.Tensor | None = None, events: list | None = None) -> torch.Tensor:
+        """Routed forward.  ``events``: optional list; when given, (name, start,
+        end) CUDA-event pairs recorded on the current stream around each grouped
+        GEMM are appended to it (used for per-kernel timing)."""
+        T, H = x.shape
+        if T > self.max_tokens:
+            self._alloc(T)
+        k = self.topk
+        if H != self.H or tuple(topk_ids.shape) != (T, k):
+            raise ValueError("x must be [T, H] and topk_ids [T, topk]")
+        R = T * k
+        dev = x.device
+        lib = _lib.load()
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        ids = topk_ids if topk_ids.dtype == torch.int32 else topk_ids.to(torch.int32)
+        ids = ids.contiguous()
+        rc = lib.w4a8_moe_align(ids.data_ptr(), T, k, self.E, self.align_block, self.offsets.data_ptr(),
+                                self.sorted_ids.data_ptr(), self.inv_pos.data_ptr(), self.padded_ids.data_ptr(),
+                                self.block_expert.data_ptr(), self.num_post_pad.data_ptr(), self.ws.data_ptr(),
+                                self.ws.numel(), stream)
+        _lib.check(rc, "moe_align")
+        xq, xs = self.xq[:R], self.xs[:R]
+        ops.quant_scatter(x, self.inv_pos[:R], k, xq, xs)
+        h = self.h[:R]
+        ev = _Ev(events)
+        ev.start("gemm_gate_up")
+        ops.w4a8_group_gemm_moe(xq, xs, self.w13.packed, self.w13.scale, self.w13.zero, self.offsets, h, self.gs)
+        ev.stop()
+        if self.ffn:
+            aq, as_ = self.aq[:R], self.as_[:R]
+            ops.silu_mul_requant(h, aq, as_)
+            y = self.y[:R]
+            ev.start("gemm_down")
+            ops.w4a8_group_gemm_moe(aq, as_, self.w2.packed, self.w2.scale, self.w2.zero, self.offsets, y,
+                                    self.gs)
+            ev.stop()
+        else:
+            y = h
+        if out is None:
+            out = self.out[:T]
+        return ops.moe_combine(y, self.inv_pos[:R], topk_weights, out)
+
+    __call__ = forward
+
+
+def w4a8_moe(x, topk_ids, topk_weights, w13: W4A8Weights, w2: W4A8Weights | None, group_size: int):
+    """One-shot routed MoE forward (allocates its buffers; use MoELayer in a loop)."""
+    layer = MoELayer(w13, w2, group_size, topk_ids.shape[1], x.shape[0])
+    return layer(x, topk_ids, topk_weights).clone()

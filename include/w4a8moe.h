@@ -1,0 +1,148 @@
+/*
+ * w4a8moe.h -- C ABI of the B200 (sm_100a) W4A8 Mixture-of-Experts library.
+ *
+ * Plain pointers, sizes and strides; every pointer is CUDA device memory on
+ * the current device unless stated otherwise; `stream` is a cudaStream_t
+ * (NULL = legacy default stream).  Nothing here allocates device memory:
+ * scratch space is passed in by the caller.  No call synchronises the host
+ * except w4a8_device_status().
+ *
+ * Return value: W4A8_OK, or an error code; w4a8_last_error() then returns a
+ * message for the calling thread.
+ *
+ * The reference ("CaiJichang212/flagos-kernel-gen", Task 1) is a Python/Triton
+ * operator; each entry point below names the reference interface it replaces.
+ */
+#ifndef W4A8MOE_H_
+#define W4A8MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define W4A8_OK 0
+#define W4A8_ERR_INVALID 1 /* bad shape, stride, alignment or argument */
+#define W4A8_ERR_CUDA 2    /* CUDA runtime / launch error */
+#define W4A8_ERR_DEVICE 3  /* a kernel reported an error in the device status word */
+
+/* Kernel selector for w4a8_group_gemm_moe_ex. */
+#define W4A8_KERNEL_AUTO 0 /* tensor-core kernel where its shape rules hold, else CUDA cores */
+#define W4A8_KERNEL_TC 1   /* TMA + tcgen05.mma.kind::i8 kernel (K >= 128, 16-byte aligned x_q rows) */
+#define W4A8_KERNEL_SIMT 2 /* dp4a CUDA-core kernel (any shape; 4-byte aligned x_q rows) */
+
+int w4a8_abi_version(void);
+const char* w4a8_last_error(void);
+
+/*
+ * Grouped W4A8 GEMM over expert segments.
+ * Replaces: w4a8_group_gemm_moe(x_q, x_scale, w_q4_packed, w_scale, w_zero,
+ *           expert_offsets, out, group_size)   docs/Task1.md:8-17 (reference
+ *           implementation docs/Task1.md:53-114; Triton launcher
+ *           Task1/v1.6/task1-codex5.5-all-v1.6.py:986-1030).
+ *   x_q            int8  [M_total, K], row stride x_stride0 (elements), unit column stride
+ *   x_scale        fp32  [M_total]
+ *   w_q4_packed    uint8 [E, N, K/2] contiguous; low nibble = even k, high = odd k
+ *   w_scale        fp32  [E, N, K/group_size] contiguous
+ *   w_zero         int8  [E, N, K/group_size] contiguous
+ *   expert_offsets int32 [E+1]: rows [off[e], off[e+1]) belong to expert e
+ *   out            bf16  [M_total, N] with strides (out_stride0, out_stride1) in elements;
+ *                  rows outside every segment are not written
+ *   group_size     64 or 128; K % group_size == 0
+ */
+int w4a8_group_gemm_moe(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
+                        const uint8_t* w_q4_packed, const float* w_scale, const int8_t* w_zero,
+                        const int32_t* expert_offsets, void* out, int64_t out_stride0,
+                        int64_t out_stride1, int64_t M_total, int64_t E, int64_t N, int64_t K,
+                        int64_t group_size, void* stream);
+
+/*
+ * Same as w4a8_group_gemm_moe with an explicit kernel choice and an optional
+ * export of the exact int32 per-group partial sums
+ *   partials[m, n, g] = sum_{k in group g} x_q[m,k] * int8(nibble - zero)
+ * (int32 [M_total, N, K/group_size], written for rows inside a segment; NULL
+ * to skip).  Replaces the per-group einsum of docs/Task1.md:100-104, which the
+ * reference keeps internal.
+ */
+int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
+                           const uint8_t* w_q4_packed, const float* w_scale, const int8_t* w_zero,
+                           const int32_t* expert_offsets, void* out, int64_t out_stride0,
+                           int64_t out_stride1, int64_t M_total, int64_t E, int64_t N, int64_t K,
+                           int64_t group_size, int32_t kernel, int32_t* partials, void* stream);
+
+/*
+ * Per-token symmetric int8 quantisation of bf16 activations.
+ * No counterpart kernel in the reference (its entry point takes x_q/x_scale
+ * already quantised, docs/Task1.md:9-10); the convention is the repository's
+ * int8 quantiser, docs/Task3.md:58-67:
+ *   x_scale[t] = max(max_k |x[t,k]| / 127, 1e-10);  x_q = trunc(clamp(x / x_scale, -127, 127))
+ *   x bf16 [T, H] (row stride x_stride0), x_q int8 [T, H] (row stride q_stride0), x_scale fp32 [T]
+ */
+int w4a8_act_quant(const void* x, int64_t x_stride0, int64_t T, int64_t H, int8_t* x_q,
+                   int64_t q_stride0, float* x_scale, void* stream);
+
+/*
+ * Fused quantise + dispatch: quantises token t once (as w4a8_act_quant) and
+ * writes it to rows inv_pos[t*topk + j] (j < topk) of x_sorted / xs_sorted,
+ * i.e. straight into expert-sorted order.  inv_pos comes from w4a8_moe_align;
+ * entries < 0 are skipped.  No reference counterpart.
+ *   x_sorted int8 [T*topk, H] contiguous, xs_sorted fp32 [T*topk]
+ */
+int w4a8_quant_scatter(const void* x, int64_t x_stride0, int64_t T, int64_t H,
+                       const int32_t* inv_pos, int64_t topk, int8_t* x_sorted, float* xs_sorted,
+                       void* stream);
+
+/* Bytes of scratch device memory w4a8_moe_align needs. */
+size_t w4a8_moe_align_workspace_size(int64_t T, int64_t topk, int64_t E);
+
+/*
+ * Token-to-expert sort and block alignment (counting sort, deterministic).
+ * No reference counterpart (the reference takes expert_offsets as input,
+ * docs/Task1.md:15); the padded outputs follow the moe_align_block_size
+ * convention (sentinel = T*topk for padding).
+ *   topk_ids       int32 [T, topk]  expert of each (token, slot); ids outside [0,E) are dropped
+ *   expert_offsets int32 [E+1]      unpadded segment starts
+ *   sorted_ids     int32 [T*topk]   flat index t*topk+j per sorted row; ascending inside an expert
+ *   inv_pos        int32 [T*topk]   sorted row of each flat index (-1 if dropped)
+ *   padded_ids     int32 [T*topk + E*(block_size-1)] or NULL
+ *   block_expert   int32 [ceil((T*topk + E*(block_size-1)) / block_size)] or NULL (-1 past the end)
+ *   num_post_pad   int32 [1] or NULL
+ *   workspace      >= w4a8_moe_align_workspace_size(T, topk, E) bytes
+ */
+int w4a8_moe_align(const int32_t* topk_ids, int64_t T, int64_t topk, int64_t E, int64_t block_size,
+                   int32_t* expert_offsets, int32_t* sorted_ids, int32_t* inv_pos,
+                   int32_t* padded_ids, int32_t* block_expert, int32_t* num_post_pad,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * SiLU-mul + per-row int8 requantisation between the gate/up and down GEMMs.
+ * No reference kernel; formula of docs/Task3.md:99-110 (gate = h[:, :I],
+ * up = h[:, I:], y = silu(gate) * up in fp32) and the quantiser of
+ * docs/Task3.md:58-67.
+ *   h bf16 [R, 2I] (row stride h_stride0) -> q int8 [R, I] contiguous, s fp32 [R]
+ */
+int w4a8_silu_mul_requant(const void* h, int64_t h_stride0, int64_t R, int64_t I, int8_t* q,
+                          float* s, void* stream);
+
+/*
+ * Weighted top-k combine back to token order (no reference counterpart):
+ *   out[t, :] = bf16( sum_{j=0..topk-1} topk_w[t,j] * y[inv_pos[t*topk+j], :] )  (fp32, j ascending)
+ *   y bf16 [*, H] (row stride y_stride0), topk_w fp32 [T, topk], out bf16 [T, H] (row stride out_stride0)
+ */
+int w4a8_moe_combine(const void* y, int64_t y_stride0, const int32_t* inv_pos, const float* topk_w,
+                     int64_t T, int64_t topk, int64_t H, void* out, int64_t out_stride0,
+                     void* stream);
+
+/*
+ * Reads (and, if reset != 0, clears) the device status word that the kernels
+ * set when a bounded wait expires.  Synchronises `stream`.  0 = healthy.
+ */
+int w4a8_device_status(int32_t* status_out, int32_t reset, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* W4A8MOE_H_ */

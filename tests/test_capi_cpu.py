@@ -1,0 +1,110 @@
+"""CPU-only checks of the drop-in boundary: the C-ABI library loads, exports
+every entry point declared in include/w4a8moe.h, validates arguments without
+touching a GPU, and the Python mirror keeps the reference's signature and
+error behaviour (docs/Task1.md:8-17, :74-75).  No compute call is made."""
+import ctypes
+import inspect
+import os
+import re
+import subprocess
+
+import pytest
+import torch
+
+from conftest import REPO
+
+HEADER = os.path.join(REPO, "include", "w4a8moe.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b(w4a8_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_expected_entry_points():
+    names = declared_functions()
+    for required in ("w4a8_group_gemm_moe", "w4a8_group_gemm_moe_ex", "w4a8_act_quant", "w4a8_quant_scatter",
+                     "w4a8_moe_align", "w4a8_moe_align_workspace_size", "w4a8_silu_mul_requant",
+                     "w4a8_moe_combine", "w4a8_device_status", "w4a8_last_error", "w4a8_abi_version"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    from importlib import import_module
+    lib_mod = import_module("flagos-kernel-gen_b200._lib")
+    lib = lib_mod.load()
+    out = subprocess.run(["nm", "-D", "--defined-only", lib_mod.LIB_PATH], capture_output=True, text=True).stdout
+    exported = set(re.findall(r"\bT\s+(w4a8_\w+)", out))
+    for name in declared_functions():
+        assert name in exported, f"{name} declared in the header but not exported"
+        assert hasattr(lib, name)
+        assert name in lib_mod.SIGNATURES, f"{name} has no ctypes signature"
+    assert lib.w4a8_abi_version() == 1
+
+
+def _call_gemm(lib, **over):
+    args = dict(x_q=1 << 20, x_stride0=512, x_scale=1 << 20, w=1 << 20, ws=1 << 20, wz=1 << 20, off=1 << 20,
+                out=1 << 20, os0=512, os1=1, M=32, E=4, N=512, K=512, gs=128, kernel=0, partials=None, stream=None)
+    args.update(over)
+    return lib.w4a8_group_gemm_moe_ex(*args.values())
+
+
+def test_capi_rejects_bad_arguments_without_a_gpu(pkg):
+    from importlib import import_module
+    L = import_module("flagos-kernel-gen_b200._lib")
+    lib = L.load()
+    assert _call_gemm(lib, gs=96) == L.W4A8_ERR_INVALID
+    assert b"group_size" in lib.w4a8_last_error()
+    assert _call_gemm(lib, K=448) == L.W4A8_ERR_INVALID           # 448 % 128 != 0
+    assert b"group_size" in lib.w4a8_last_error()
+    assert _call_gemm(lib, x_stride0=100) == L.W4A8_ERR_INVALID   # stride < K
+    assert _call_gemm(lib, kernel=7) == L.W4A8_ERR_INVALID
+    assert _call_gemm(lib, w=None) == L.W4A8_ERR_INVALID
+    # nothing to do is not an error
+    assert _call_gemm(lib, M=0) == L.W4A8_OK
+    ws = ctypes.c_size_t(lib.w4a8_moe_align_workspace_size(16, 8, 256)).value
+    assert ws >= 4 * (256 + 128)
+    assert lib.w4a8_moe_align(None, 16, 8, 256, 128, 1 << 20, 1 << 20, 1 << 20, None, None, None, 1 << 20, 4,
+                              None) == L.W4A8_ERR_INVALID
+    assert b"workspace" in lib.w4a8_last_error() or b"null" in lib.w4a8_last_error()
+
+
+def test_python_signature_matches_reference(pkg):
+    sig = inspect.signature(pkg.w4a8_group_gemm_moe)
+    assert list(sig.parameters) == ["x_q", "x_scale", "w_q4_packed", "w_scale", "w_zero", "expert_offsets", "out",
+                                    "group_size"]
+
+
+def test_reference_asserts_are_kept(pkg):
+    E, N, K, M, gs = 2, 128, 256, 8, 128
+    x_q = torch.zeros((M, K), dtype=torch.int8)
+    xs = torch.ones(M)
+    w_bad = torch.zeros((E, N, K // 2 + 1), dtype=torch.uint8)
+    wsc = torch.ones((E, N, K // gs))
+    wz = torch.zeros((E, N, K // gs), dtype=torch.int8)
+    off = torch.tensor([0, 4, 8], dtype=torch.int32)
+    out = torch.zeros((M, N), dtype=torch.bfloat16)
+    with pytest.raises(AssertionError):                 # K_half * 2 == K  (docs/Task1.md:74)
+        pkg.w4a8_group_gemm_moe(x_q, xs, w_bad, wsc, wz, off, out, gs)
+    w = torch.zeros((E, N, K // 2), dtype=torch.uint8)
+    with pytest.raises(AssertionError):                 # K % group_size == 0  (docs/Task1.md:75)
+        pkg.w4a8_group_gemm_moe(x_q, xs, w, wsc, wz, off, out, 96)
+
+
+def test_no_cpu_fallback(pkg):
+    E, N, K, M, gs = 2, 128, 256, 8, 128
+    args = (torch.zeros((M, K), dtype=torch.int8), torch.ones(M), torch.zeros((E, N, K // 2), dtype=torch.uint8),
+            torch.ones((E, N, K // gs)), torch.zeros((E, N, K // gs), dtype=torch.int8),
+            torch.tensor([0, 4, 8], dtype=torch.int32), torch.zeros((M, N), dtype=torch.bfloat16), gs)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        pkg.w4a8_group_gemm_moe(*args)
+
+
+def test_product_path_never_imports_the_oracle():
+    pkg_dir = os.path.join(REPO, "flagos-kernel-gen_b200")
+    for root, _, files in os.walk(pkg_dir):
+        for f in files:
+            if f.endswith((".py", ".cu", ".cuh", ".h")):
+                text = open(os.path.join(root, f), encoding="utf-8").read()
+                assert "import oracle" not in text and "from oracle" not in text, f

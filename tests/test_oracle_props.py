@@ -1,0 +1,93 @@
+"""Properties of the oracle's restatements that have no reference code (align,
+combine, quantiser edge cases), and of the seeded workloads."""
+import numpy as np
+import pytest
+import torch
+from hypothesis import given, settings, strategies as st
+
+
+@settings(max_examples=40, deadline=None)
+@given(T=st.integers(0, 40), k=st.integers(1, 8), E=st.integers(1, 20), bs=st.sampled_from([1, 16, 64, 128]),
+       seed=st.integers(0, 1000), drop=st.booleans())
+def test_align_is_a_stable_counting_sort(O, T, k, E, bs, seed, drop):
+    rng = np.random.default_rng(seed)
+    lo = -1 if drop else 0
+    ids = rng.integers(lo, E + (1 if drop else 0), size=(T, k)).astype(np.int32)
+    a = O.moe_align(ids, E, bs)
+    flat = ids.reshape(-1)
+    valid = (flat >= 0) & (flat < E)
+    off = a["expert_offsets"]
+    assert off[0] == 0 and off[-1] == valid.sum()
+    for e in range(E):
+        seg = a["sorted_ids"][off[e]:off[e + 1]]
+        assert (flat[seg] == e).all()
+        assert (np.diff(seg) > 0).all()          # stable: ascending flat index
+    inv = a["inv_pos"]
+    assert (inv[~valid] == -1).all()
+    np.testing.assert_array_equal(a["sorted_ids"][inv[valid]], np.nonzero(valid)[0])
+    # padded form
+    R = T * k
+    cap = R + E * (bs - 1)
+    assert a["padded_ids"].shape[0] == cap
+    assert a["num_post_pad"] % bs == 0
+    real = a["padded_ids"][a["padded_ids"] != R]
+    np.testing.assert_array_equal(np.sort(real), np.sort(a["sorted_ids"]))
+    for b, e in enumerate(a["block_expert"]):
+        rows = a["padded_ids"][b * bs:(b + 1) * bs]
+        rows = rows[rows != R]
+        if e < 0:
+            assert b * bs >= a["num_post_pad"] and rows.size == 0
+        else:
+            assert (flat[rows] == e).all()
+
+
+def test_combine_is_the_weighted_sum(O):
+    rng = np.random.default_rng(0)
+    T, k, H = 5, 3, 16
+    y = torch.from_numpy(rng.standard_normal((T * k, H)).astype(np.float32)).to(torch.bfloat16)
+    w = rng.random((T, k)).astype(np.float32)
+    inv = rng.permutation(T * k).astype(np.int32)
+    out = O.combine(y, inv, w)
+    yf = y.to(torch.float32).numpy()
+    ref = np.zeros((T, H), np.float32)
+    for t in range(T):
+        for j in range(k):
+            ref[t] = ref[t] + np.float32(w[t, j]) * yf[inv[t * k + j]]
+    np.testing.assert_array_equal(out.to(torch.float32).numpy(), torch.from_numpy(ref).to(torch.bfloat16).float().numpy())
+
+
+def test_quantiser_edge_cases(O):
+    x = torch.zeros((3, 256), dtype=torch.bfloat16)
+    x[1, 0] = -5.0
+    x[2] = torch.linspace(-1, 1, 256).to(torch.bfloat16)
+    q, s = O.act_quant(x)
+    assert s[0] == np.float32(1e-10) and (q[0] == 0).all()
+    assert q[1, 0] == -127 and (q[1, 1:] == 0).all()
+    assert q.min() >= -127 and q.max() <= 127
+    # truncation toward zero, not rounding
+    y = np.array([[127.0, 0.99, -0.99, 1.5, -1.5]], np.float32)
+    qq, ss = O.quant_rows(y)
+    assert ss[0] == 1.0 and list(qq[0]) == [127, 0, 0, 1, -1]
+
+
+def test_workload_generators(pkg):
+    W = pkg.workloads
+    for name, cfg in W.CONFIGS.items():
+        if cfg.experts * cfg.hidden * cfg.inter > 2 ** 28:
+            continue
+        inp = W.make_moe_inputs(cfg, 32, seed=0)
+        assert inp.topk_ids.shape == (32, cfg.topk) and inp.topk_ids.dtype == torch.int32
+        torch.testing.assert_close(inp.topk_weights.sum(-1), torch.ones(32))
+        packed, scale, zero = inp.w13
+        assert packed.dtype == torch.uint8 and (zero == 8).all()
+        assert float(scale.min()) >= 0.005 and float(scale.max()) <= 0.02
+    off = W.random_splits(16, 100, W.make_generator(0))
+    assert off[0] == 0 and off[-1] == 100 and (off[1:] >= off[:-1]).all()
+
+
+def test_zipf_routing_is_skewed(pkg):
+    W = pkg.workloads
+    cfg = W.CONFIGS["qwen3_zipf"]
+    inp = W.make_moe_inputs(cfg, 1024, seed=0, weights=False)
+    counts = np.bincount(inp.topk_ids.numpy().reshape(-1), minlength=cfg.experts)
+    assert counts.max() > 10 * np.median(counts)
