@@ -233,6 +233,43 @@ def build_layer(pkg, cfg, T, rank, world, dev):
     return ep.ExpertParallelMoE.with_synthetic_weights(cfg, T, rank, world, dev, gen)
 
 
+def kernel_bench(pkg, spec: str, steps: int, warmup: int, kernel: int):
+    """Kernel-only mode: one grouped GEMM launch per step on the 8-argument
+    operator (E experts x M rows each, N x K weights, group 128), e.g.
+    ``--workload gemm_E32_M256_N4096_K7168``.  Used for ncu captures."""
+    m = re.fullmatch(r"gemm_E(\d+)_M(\d+)_N(\d+)_K(\d+)(?:_G(\d+))?", spec)
+    E, M, N, K = (int(m.group(i)) for i in range(1, 5))
+    gs = int(m.group(5) or 128)
+    W = pkg.workloads
+    dev = torch.device("cuda", 0)
+    gen = W.make_generator(0, dev)
+    w, ws, wz = W.make_int4_weights(E, N, K, gs, gen, dev)
+    R = E * M
+    x_q = torch.randint(-127, 128, (R, K), generator=gen, device=dev, dtype=torch.int8)
+    xs = torch.empty((R,), device=dev).uniform_(0.001, 0.05, generator=gen)
+    off = torch.arange(0, R + 1, M, device=dev, dtype=torch.int32)
+    out = torch.empty((R, N), dtype=torch.bfloat16, device=dev)
+    for _ in range(warmup):
+        pkg.w4a8_group_gemm_moe_ex(x_q, xs, w, ws, wz, off, out, gs, kernel=kernel)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        pkg.w4a8_group_gemm_moe_ex(x_q, xs, w, ws, wz, off, out, gs, kernel=kernel)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    peaks = load_peaks()
+    byts = W.gemm_roofline_bytes(E, R, N, K, gs)
+    ops_ = W.gemm_ops(R, N, K)
+    print(json.dumps({"metric": "grouped GEMM rows/s", "value": R / (ms * 1e-3), "unit": "rows/s",
+                      "ms_per_launch": ms, "workload": spec, "kernel": kernel, "steps": steps,
+                      "hbm_frac": byts / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                      "int8_frac": ops_ / (ms * 1e-3) / 1e12 / (2 * peaks["bf16_tflops"]),
+                      "GBps": byts / (ms * 1e-3) / 1e9, "TOPS": ops_ / (ms * 1e-3) / 1e12,
+                      "device_status": pkg.device_status()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -243,7 +280,11 @@ def main():
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=6.0, help="seconds of CPU work per baseline step")
+    ap.add_argument("--kernel", type=int, default=0, help="kernel-only mode: 0 auto, 1 tensor core, 2 CUDA core")
     args = ap.parse_args()
+    if args.workload.startswith("gemm_"):
+        kernel_bench(importlib.import_module(PKG_NAME), args.workload, args.steps, args.warmup, args.kernel)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

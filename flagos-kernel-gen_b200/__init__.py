@@ -14,6 +14,7 @@ from .ops import (  # noqa: F401
     act_quant,
     align_capacity,
     device_status,
+    gather_rows,
     moe_align,
     moe_combine,
     quant_scatter,
@@ -27,6 +28,6 @@ from . import workloads  # noqa: F401
 
 __all__ = [
     "w4a8_group_gemm_moe", "w4a8_group_gemm_moe_ex", "act_quant", "moe_align", "quant_scatter",
-    "silu_mul_requant", "moe_combine", "device_status", "MoELayer", "W4A8Weights", "w4a8_moe",
+    "silu_mul_requant", "moe_combine", "gather_rows", "device_status", "MoELayer", "W4A8Weights", "w4a8_moe",
     "KERNEL_AUTO", "KERNEL_TC", "KERNEL_SIMT", "workloads",
 ]

@@ -23,6 +23,8 @@ cudaError_t launch_moe_align(const int32_t* ids, int R, int E, int bs, int32_t* 
 cudaError_t launch_silu_mul_requant(const __nv_bfloat16* h, int64_t h_stride0, int R, int I, int8_t* q,
                                     int64_t q_stride0, float* s, const int32_t* valid_rows,
                                     cudaStream_t stream);
+cudaError_t launch_gather_rows(const void* src, int64_t src_stride, const int32_t* index, int64_t rows,
+                               int64_t row_bytes, void* dst, int64_t dst_stride, cudaStream_t stream);
 cudaError_t launch_moe_combine(const __nv_bfloat16* y, int64_t y_stride0, const int32_t* inv_pos,
                                const float* topk_w, int T, int topk, int H, __nv_bfloat16* out,
                                int64_t out_stride0, cudaStream_t stream);
@@ -131,7 +133,7 @@ int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_
   a.K = static_cast<int>(K);
   a.gs = static_cast<int>(group_size);
 
-  const bool tc_ok = K >= 128 && (reinterpret_cast<uintptr_t>(x_q) % 16 == 0) && (x_stride0 % 16 == 0) &&
+  const bool tc_ok = gemm_tc_supports((int)K, (int)group_size, (int)E) && (reinterpret_cast<uintptr_t>(x_q) % 16 == 0) && (x_stride0 % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(w_q4_packed) % 16 == 0);
   const bool simt_ok = (reinterpret_cast<uintptr_t>(x_q) % 4 == 0) && (x_stride0 % 4 == 0);
   int use = kernel;
@@ -141,7 +143,7 @@ int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_
   if (use == W4A8_KERNEL_TC) {
     if (!tc_ok)
       return fail(W4A8_ERR_INVALID,
-                  "tensor-core kernel needs K >= 128 and 16-byte aligned x_q rows / weights");
+                  "tensor-core kernel needs K >= 128, E <= 1024 and 16-byte aligned x_q rows / weights");
     e = launch_gemm_tc(a, st);
   } else if (use == W4A8_KERNEL_SIMT) {
     if (!simt_ok) return fail(W4A8_ERR_INVALID, "CUDA-core kernel needs 4-byte aligned x_q rows");
@@ -238,6 +240,18 @@ int w4a8_moe_combine(const void* y, int64_t y_stride0, const int32_t* inv_pos, c
                                      (int)topk, (int)H, static_cast<__nv_bfloat16*>(out), out_stride0,
                                      static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? W4A8_OK : cuda_fail(e, "moe_combine launch");
+}
+
+int w4a8_gather_rows(const void* src, int64_t src_stride_bytes, const int32_t* index, int64_t rows,
+                     int64_t row_bytes, void* dst, int64_t dst_stride_bytes, void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+  if (rows < 0 || rows > INT32_MAX || row_bytes < 0 || src_stride_bytes < row_bytes || dst_stride_bytes < row_bytes)
+    return fail(W4A8_ERR_INVALID, "bad sizes rows=%lld row_bytes=%lld", (long long)rows, (long long)row_bytes);
+  if (rows == 0 || row_bytes == 0) return W4A8_OK;
+  if (src == nullptr || index == nullptr || dst == nullptr) return fail(W4A8_ERR_INVALID, "null pointer");
+  cudaError_t e = launch_gather_rows(src, src_stride_bytes, index, rows, row_bytes, dst, dst_stride_bytes,
+                                     static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? W4A8_OK : cuda_fail(e, "gather_rows launch");
 }
 
 int w4a8_device_status(int32_t* status_out, int32_t reset, void* stream) {

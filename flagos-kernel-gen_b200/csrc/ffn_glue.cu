@@ -127,7 +127,35 @@ moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int64_t y_stride0, const
   }
 }
 
+// dst row i = src row index[i] (row_bytes bytes each); index < 0 leaves dst row i untouched.
+__global__ void __launch_bounds__(kGThreads)
+gather_rows_kernel(const uint8_t* __restrict__ src, int64_t src_stride, const int32_t* __restrict__ index,
+                   int64_t row_bytes, uint8_t* __restrict__ dst, int64_t dst_stride, bool vec16) {
+  const int64_t i = blockIdx.x;
+  const int j = index[i];
+  if (j < 0) return;
+  const uint8_t* s = src + static_cast<int64_t>(j) * src_stride;
+  uint8_t* d = dst + i * dst_stride;
+  if (vec16) {
+    const int64_t n = row_bytes / 16;
+    for (int64_t c = threadIdx.x; c < n; c += kGThreads)
+      reinterpret_cast<uint4*>(d)[c] = __ldg(reinterpret_cast<const uint4*>(s) + c);
+  } else {
+    for (int64_t c = threadIdx.x; c < row_bytes; c += kGThreads) d[c] = s[c];
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_gather_rows(const void* src, int64_t src_stride, const int32_t* index, int64_t rows,
+                               int64_t row_bytes, void* dst, int64_t dst_stride, cudaStream_t stream) {
+  if (rows <= 0 || row_bytes <= 0) return cudaSuccess;
+  const bool vec16 = (row_bytes % 16 == 0) && (src_stride % 16 == 0) && (dst_stride % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(src) % 16 == 0) && (reinterpret_cast<uintptr_t>(dst) % 16 == 0);
+  gather_rows_kernel<<<static_cast<unsigned>(rows), kGThreads, 0, stream>>>(
+      static_cast<const uint8_t*>(src), src_stride, index, row_bytes, static_cast<uint8_t*>(dst), dst_stride, vec16);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_silu_mul_requant(const __nv_bfloat16* h, int64_t h_stride0, int R, int I, int8_t* q,
                                     int64_t q_stride0, float* s, const int32_t* valid_rows,

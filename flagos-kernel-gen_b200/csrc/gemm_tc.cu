@@ -8,24 +8,30 @@
 // for every row m of expert e's segment [off[e], off[e+1]).
 //
 // Design (swap-AB): the MMA's M dimension is 128 weight rows (output
-// channels) and its N dimension is the token block (16..128 rows of the
+// channels) and its N dimension is the token block (16..256 rows of the
 // expert's segment, rounded up to 16 per tile at run time).  With weights on
-// the M side, every epilogue thread owns one output channel, so the per-group
-// weight scale is a single register per thread and the int32 -> fp32 scale
-// step is one FMA per element.
+// the M side every epilogue thread owns one output channel, so the per-group
+// weight scale is one register per thread.
 //
-// Warp roles (448 threads, one CTA per SM, persistent over tiles):
-//   warp 0      TMA producer: packed weight tile [128 rows x 64 B] and the
-//               token tile [rows x 128 B] (128-byte swizzle) per 128-wide K block
+// Exact int32 -> fp32 without I2F: before a group's first MMA each TMEM
+// accumulator holds the bit pattern of 1.5 * 2^23 (0x4B400000).  The MMAs add
+// the integer partial P to those bits; for |P| < 2^22 (|P| <= 2^21 here) the
+// result, read as fp32, is exactly 1.5 * 2^23 + P, so one exact FADD recovers
+// float(P).  Scale accumulation then uses packed fp32x2 FADD/FFMA, which round
+// exactly like the scalar fmaf of the CUDA-core kernel (both kernels produce
+// identical bits).
+//
+// Warp roles (512 threads, one CTA per SM, persistent over tiles):
+//   warp 0      TMA producer of token tiles [rows x 128 B] (128-byte swizzle)
 //   warp 1      TMEM allocator + single-thread MMA issuer
-//   warps 2-5   transform: thread r unpacks weight row r (nibble order of
-//               docs/Task1.md:78-81, zero fold with int8 wrap of :84-85) into the
-//               canonical 128B-swizzled K-major layout the MMA reads
-//   warps 6-13  epilogue: two warpgroups, each reads 64 token columns of the
-//               per-group int32 accumulator from TMEM, applies w_scale, and
-//               finally x_scale and the bf16 store
-// TMEM holds two 128-column int32 accumulators so that group g+1's MMAs run
-// while the epilogue drains group g.
+//   warp 2      TMA producer of packed weight tiles [128 rows x 64 B] (64-byte
+//               swizzle), running ahead on its own deeper ring
+//   warps 4-7   transform: thread r unpacks weight row r (nibble order of
+//               docs/Task1.md:78-81, zero fold with the int8 wrap of :84-85)
+//               into the canonical 128B-swizzled K-major layout the MMA reads
+//   warps 8-15  epilogue: two warpgroups of 128 token columns each
+// Register split (setmaxnreg): warpgroups 0-1 drop to 56, the epilogue
+// warpgroups rise to 200: 2*128*56 + 2*128*200 = 65536 = the launch's 512 x 128.
 #include "common.cuh"
 #include "w4a8_internal.h"
 
@@ -37,25 +43,29 @@ namespace w4a8 {
 namespace {
 
 constexpr int kBW = 128;         // weight rows per tile (MMA M)
-constexpr int kBT = 128;         // max token rows per tile (MMA N)
+constexpr int kBT = 256;         // max token rows per tile (MMA N)
 constexpr int kBK = 128;         // K bytes per pipeline stage
-constexpr int kStages = 4;       // TMA stages (packed weights + tokens)
-constexpr int kAStages = 2;      // unpacked weight stages
-constexpr int kXBytes = kBT * kBK;          // 16 KB
+constexpr int kXStages = 3;      // token tile ring
+constexpr int kWStages = 8;      // packed weight ring
+constexpr int kAStages = 2;      // unpacked weight ring
+constexpr int kXBytes = kBT * kBK;          // 32 KB
 constexpr int kABytes = kBW * kBK;          // 16 KB
 constexpr int kWBytes = kBW * (kBK / 2);    // 8 KB
-constexpr int kThreads = 448;
-constexpr int kTmemCols = 256;   // 2 accumulators x 128 columns
+constexpr int kThreads = 512;
+constexpr int kTmemCols = 512;   // 2 accumulators x 256 columns
 constexpr int kXBoxRows = 16;
+constexpr int kMaxExperts = 1024;
 
-constexpr int kTransformWarp0 = 2;
-constexpr int kEpilogueWarp0 = 6;
+constexpr int kTransformWarp0 = 4;
+constexpr int kEpilogueWarp0 = 8;
 constexpr int kNumEpilogueWarps = 8;
 constexpr int kEpiCols = kBT / 2;           // columns per epilogue warpgroup
+constexpr uint32_t kMagicBits = 0x4B400000u;  // 1.5 * 2^23
+constexpr float kMagic = 12582912.0f;
 
-constexpr size_t kSmemTiles = size_t(kStages) * kXBytes + size_t(kAStages) * kABytes +
-                              size_t(kStages) * kWBytes;
-constexpr int kNumBars = 2 * kStages + 2 * kAStages + 4;
+constexpr size_t kSmemTiles = size_t(kXStages) * kXBytes + size_t(kAStages) * kABytes +
+                              size_t(kWStages) * kWBytes;
+constexpr int kNumBars = 2 * kXStages + 2 * kWStages + 2 * kAStages + 4;
 
 __host__ __device__ constexpr size_t tc_smem_bytes(int E) {
   return 1024 /*alignment slack*/ + kSmemTiles + kNumBars * 8 + 16 + sizeof(int) * 3 * (E + 1);
@@ -67,6 +77,49 @@ __device__ __forceinline__ uint32_t pack_fold(uint32_t nib4, uint32_t c7, uint32
   return (nib4 + c7) ^ c8;
 }
 
+__device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// Store the same 32-bit value to 32 consecutive columns of this warp's lanes.
+__device__ __forceinline__ void tmem_st_x32_fill(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+      "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+      "r"(v)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
+}
+__device__ __forceinline__ uint64_t u2_pack(uint32_t lo, uint32_t hi) {
+  return static_cast<uint64_t>(lo) | (static_cast<uint64_t>(hi) << 32);
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                const GemmArgs a) {
@@ -74,12 +127,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sX = base;
-  uint8_t* sA = sX + kStages * kXBytes;
+  uint8_t* sA = sX + kXStages * kXBytes;
   uint8_t* sW = sA + kAStages * kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + kStages * kWBytes);
-  uint64_t* load_full = bars;
-  uint64_t* load_empty = load_full + kStages;
-  uint64_t* a_full = load_empty + kStages;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + kWStages * kWBytes);
+  uint64_t* x_full = bars;
+  uint64_t* x_empty = x_full + kXStages;
+  uint64_t* w_full = x_empty + kXStages;
+  uint64_t* w_empty = w_full + kWStages;
+  uint64_t* a_full = w_empty + kWStages;
   uint64_t* a_empty = a_full + kAStages;
   uint64_t* tmem_full = a_empty + kAStages;
   uint64_t* tmem_empty = tmem_full + 2;
@@ -91,9 +146,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   const int lane = lane_id();
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&load_full[s], 1);
-      mbar_init(&load_empty[s], 4 + 1);  // 4 transform warps + 1 MMA commit
+    for (int s = 0; s < kXStages; ++s) {
+      mbar_init(&x_full[s], 1);
+      mbar_init(&x_empty[s], 1);   // MMA commit
+    }
+    for (int s = 0; s < kWStages; ++s) {
+      mbar_init(&w_full[s], 1);
+      mbar_init(&w_empty[s], 4);   // 4 transform warps
     }
     for (int s = 0; s < kAStages; ++s) {
       mbar_init(&a_full[s], 4);
@@ -122,35 +181,71 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Epilogue warps seed both accumulators with the magic bits before any MMA.
+  if (warp >= kEpilogueWarp0) {
+    const int quarter = warp & 3;
+    const int wg = (warp - kEpilogueWarp0) >> 2;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+      for (int c = 0; c < kEpiCols / 32; ++c)
+        tmem_st_x32_fill(lane_base + b * kBT + wg * kEpiCols + c * 32, kMagicBits);
+    tmem_st_wait();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+
   const int G = a.K / a.gs;
   const int KB = (a.K + kBK - 1) / kBK;
   const int gpk = kBK / a.gs;  // groups per K block: 1 (gs=128) or 2 (gs=64)
   const int kpg = a.gs / 32;   // MMA K-steps (32 bytes each) per group
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+  // Each warpgroup's branch starts with its own setmaxnreg, so the compiler
+  // allocates the code that follows within that budget.
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+   if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer: token tiles
     if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         const Tile tile = sched_tile(sch, t);
         const int nx = (tile.rows + kXBoxRows - 1) / kXBoxRows;
-        const uint32_t bytes = kWBytes + nx * kXBoxRows * kBK;
-        const int wrow = tile.e * a.N + tile.nb * kBW;
+        const uint32_t bytes = nx * kXBoxRows * kBK;
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(&load_empty[stage], phase ^ 1, a.status, kDevTimeoutLoadEmpty, abort_flag))
-            goto producer_done;
-          mbar_arrive_expect_tx(&load_full[stage], bytes);
-          tma_load_2d(sW + stage * kWBytes, &tm_w, &load_full[stage], kb * (kBK / 2), wrow, pol_w);
+          if (!mbar_wait(&x_empty[stage], phase ^ 1, a.status, kDevTimeoutLoadEmpty, abort_flag))
+            goto x_done;
+          mbar_arrive_expect_tx(&x_full[stage], bytes);
           for (int j = 0; j < nx; ++j)
-            tma_load_2d(sX + stage * kXBytes + j * kXBoxRows * kBK, &tm_x, &load_full[stage],
-                        kb * kBK, tile.m0 + j * kXBoxRows, pol_x);
-          if (++stage == kStages) { stage = 0; phase ^= 1; }
+            tma_load_2d(sX + stage * kXBytes + j * kXBoxRows * kBK, &tm_x, &x_full[stage], kb * kBK,
+                        tile.m0 + j * kXBoxRows, pol_x);
+          if (++stage == kXStages) { stage = 0; phase ^= 1; }
         }
       }
-    producer_done:;
+    x_done:;
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ TMA producer: packed weights
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        const Tile tile = sched_tile(sch, t);
+        const int wrow = tile.e * a.N + tile.nb * kBW;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&w_empty[stage], phase ^ 1, a.status, kDevTimeoutLoadEmpty, abort_flag))
+            goto w_done;
+          mbar_arrive_expect_tx(&w_full[stage], kWBytes);
+          tma_load_2d(sW + stage * kWBytes, &tm_w, &w_full[stage], kb * (kBK / 2), wrow, pol_w);
+          if (++stage == kWStages) { stage = 0; phase ^= 1; }
+        }
+      }
+    w_done:;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -159,15 +254,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
       uint32_t phase = 0, aphase = 0, bphase = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         const Tile tile = sched_tile(sch, t);
-        int n_mma = (tile.rows + 15) & ~15;
+        const int n_mma = (tile.rows + 15) & ~15;
         const uint32_t idesc = make_idesc_i8(kBW, n_mma);
         for (int g = 0; g < G; ++g) {
           const int sub = g % gpk;
           if (sub == 0) {
-            if (!mbar_wait(&load_full[stage], phase, a.status, kDevTimeoutLoadFull, abort_flag))
-              goto mma_done;
-            if (!mbar_wait(&a_full[astage], aphase, a.status, kDevTimeoutAFull, abort_flag))
-              goto mma_done;
+            if (!mbar_wait(&x_full[stage], phase, a.status, kDevTimeoutLoadFull, abort_flag)) goto mma_done;
+            if (!mbar_wait(&a_full[astage], aphase, a.status, kDevTimeoutAFull, abort_flag)) goto mma_done;
             tc_fence_after();
           }
           if (!mbar_wait(&tmem_empty[buf], bphase ^ 1, a.status, kDevTimeoutTmemEmpty, abort_flag))
@@ -178,25 +271,28 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
           const uint32_t b_addr = smem_u32(sX + stage * kXBytes);
           for (int ks = 0; ks < kpg; ++ks) {
             const uint32_t koff = static_cast<uint32_t>((sub * kpg + ks) * 32);
-            mma_i8_ss(d_tmem, make_desc_sw128(a_addr + koff), make_desc_sw128(b_addr + koff), idesc,
-                      ks > 0 ? 1u : 0u);
+            // always accumulate: the accumulator starts from the magic bits
+            mma_i8_ss(d_tmem, make_desc_sw128(a_addr + koff), make_desc_sw128(b_addr + koff), idesc, 1u);
           }
           mma_commit(&tmem_full[buf]);
           buf ^= 1;
           if (buf == 0) bphase ^= 1;
           if (sub == gpk - 1 || g == G - 1) {
-            mma_commit(&load_empty[stage]);
+            mma_commit(&x_empty[stage]);
             mma_commit(&a_empty[astage]);
-            if (++stage == kStages) { stage = 0; phase ^= 1; }
+            if (++stage == kXStages) { stage = 0; phase ^= 1; }
             if (++astage == kAStages) { astage = 0; aphase ^= 1; }
           }
         }
       }
     mma_done:;
     }
-  } else if (warp >= kTransformWarp0 && warp < kTransformWarp0 + 4) {
+   }
+  } else if (warp < kEpilogueWarp0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
     // ------------------------------------------------------------ int4 -> int8 transform
     const int r = (warp - kTransformWarp0) * 32 + lane;  // weight row within the tile
+    const int sw = (r >> 1) & 3;                         // 64-byte swizzle of the packed tile
     int stage = 0, astage = 0;
     uint32_t phase = 0, aphase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
@@ -204,45 +300,47 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
       const int n = tile.nb * kBW + r;
       const bool valid = n < a.N;
       const int8_t* zrow = a.w_zero + (static_cast<int64_t>(tile.e) * a.N + (valid ? n : 0)) * G;
+      int z0n = valid ? zrow[0] : 0;
+      int z1n = (gpk == 2 && valid && 1 < G) ? zrow[1] : z0n;
       for (int kb = 0; kb < KB; ++kb) {
-        const int g0 = kb * gpk;
-        const int z0 = valid ? zrow[g0] : 0;
-        const int z1 = (gpk == 2 && valid && g0 + 1 < G) ? zrow[g0 + 1] : z0;
-        if (!mbar_wait(&load_full[stage], phase, a.status, kDevTimeoutLoadFull, abort_flag)) goto tr_done;
-        // Packed row r (64 B) is read as four 16-byte chunks.  Register slot c
-        // holds chunk (c + rot) & 3: rotating by row pair puts the 8 lanes of a
-        // quarter-warp on 8 distinct 16-byte bank groups.
-        const int rot = (r >> 1) & 3;
+        const int z0 = z0n, z1 = z1n;
+        {  // prefetch the next K block's zero points
+          const int g0 = (kb + 1) * gpk;
+          if (valid && g0 < G) {
+            z0n = zrow[g0];
+            z1n = (gpk == 2 && g0 + 1 < G) ? zrow[g0 + 1] : z0n;
+          }
+        }
+        if (!mbar_wait(&w_full[stage], phase, a.status, kDevTimeoutLoadFull, abort_flag)) goto tr_done;
         uint4 pk[4];
         {
           const uint8_t* src = sW + stage * kWBytes + r * (kBK / 2);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) pk[c] = *reinterpret_cast<const uint4*>(src + ((c + rot) & 3) * 16);
+          for (int c = 0; c < 4; ++c) pk[c] = *reinterpret_cast<const uint4*>(src + ((c ^ sw) << 4));
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&load_empty[stage]);
-        if (++stage == kStages) { stage = 0; phase ^= 1; }
+        if (lane == 0) mbar_arrive(&w_empty[stage]);
+        if (++stage == kWStages) { stage = 0; phase ^= 1; }
 
         if (!mbar_wait(&a_empty[astage], aphase ^ 1, a.status, kDevTimeoutAEmpty, abort_flag)) goto tr_done;
         uint8_t* dst_row = sA + astage * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          // packed chunk cc (16 B) -> K offsets [32cc, 32cc+32) -> output chunks 2cc, 2cc+1
-          const int cc = (c + rot) & 3;
-          const int zc = (cc < 2) ? z0 : z1;   // gs=64: chunks 0-1 are group 2kb, 2-3 group 2kb+1
+          // packed chunk c (16 B) -> K offsets [32c, 32c+32) -> output chunks 2c, 2c+1
+          const int zc = (c < 2) ? z0 : z1;   // gs=64: chunks 0-1 are group 2kb, 2-3 group 2kb+1
           const uint32_t cb = static_cast<uint32_t>(-zc) & 0xFFu;
           const uint32_t c7 = (cb & 0x7Fu) * 0x01010101u;
           const uint32_t c8 = (cb & 0x80u) * 0x01010101u;
+          const uint32_t wv[4] = {pk[c].x, pk[c].y, pk[c].z, pk[c].w};
           uint32_t o[8];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const uint32_t wq = q == 0 ? pk[c].x : q == 1 ? pk[c].y : q == 2 ? pk[c].z : pk[c].w;
-            const uint32_t lo = wq & 0x0F0F0F0Fu;
-            const uint32_t hi = (wq >> 4) & 0x0F0F0F0Fu;
+            const uint32_t lo = wv[q] & 0x0F0F0F0Fu;
+            const uint32_t hi = (wv[q] >> 4) & 0x0F0F0F0Fu;
             o[2 * q] = pack_fold(__byte_perm(lo, hi, 0x5140), c7, c8);
             o[2 * q + 1] = pack_fold(__byte_perm(lo, hi, 0x7362), c7, c8);
           }
-          const int j0 = 2 * cc, j1 = 2 * cc + 1;
+          const int j0 = 2 * c, j1 = 2 * c + 1;
           *reinterpret_cast<uint4*>(dst_row + ((j0 ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
           *reinterpret_cast<uint4*>(dst_row + ((j1 ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
         }
@@ -253,48 +351,60 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
       }
     }
   tr_done:;
-  } else if (warp >= kEpilogueWarp0 && warp < kEpilogueWarp0 + kNumEpilogueWarps) {
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 200;");
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;                     // TMEM lane quarter this warp may access
     const int wg = (warp - kEpilogueWarp0) >> 2;      // column half
     const int r = quarter * 32 + lane;                // weight row within the tile
+    const uint64_t magic2 = f2_pack(kMagic, kMagic);
     int buf = 0;
     uint32_t bphase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const Tile tile = sched_tile(sch, t);
       const int n = tile.nb * kBW + r;
       const bool valid = n < a.N;
+      const int n_mma = (tile.rows + 15) & ~15;
+      const int my_cols = n_mma - wg * kEpiCols;      // columns of this warpgroup holding tokens (may be <= 0)
       const float* wsrow = a.w_scale + (static_cast<int64_t>(tile.e) * a.N + (valid ? n : 0)) * G;
-      float acc[kEpiCols];
+      uint64_t acc[kEpiCols / 2];
 #pragma unroll
-      for (int c = 0; c < kEpiCols; ++c) acc[c] = 0.f;
+      for (int c = 0; c < kEpiCols / 2; ++c) acc[c] = 0;
       float ws_next = valid ? __ldg(wsrow) : 0.f;
       for (int g = 0; g < G; ++g) {
         const float ws = ws_next;
         if (valid && g + 1 < G) ws_next = __ldg(wsrow + g + 1);
+        const uint64_t ws2 = f2_pack(ws, ws);
         if (!mbar_wait(&tmem_full[buf], bphase, a.status, kDevTimeoutTmemFull, abort_flag)) goto epi_done;
         tc_fence_after();
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                static_cast<uint32_t>(buf * kBT + wg * kEpiCols);
 #pragma unroll
-        for (int c16 = 0; c16 < kEpiCols / 16; ++c16) {
-          uint32_t v[16];
-          __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp must be converged
-          tmem_ld_x16(taddr + c16 * 16, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            acc[c16 * 16 + j] = fmaf(static_cast<float>(static_cast<int>(v[j])), ws, acc[c16 * 16 + j]);
-          }
-          if (a.partials != nullptr && valid) {
+        for (int c32 = 0; c32 < kEpiCols / 32; ++c32) {
+          if (c32 * 32 < my_cols) {   // warp-uniform
+            uint32_t v[32];
+            __syncwarp();
+            tmem_ld_x32(taddr + c32 * 32, v);
+            tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              const int col = wg * kEpiCols + c16 * 16 + j;
-              if (col < tile.rows)
-                a.partials[(static_cast<int64_t>(tile.m0 + col) * a.N + n) * G + g] = static_cast<int>(v[j]);
+              const uint64_t p2 = f2_sub(u2_pack(v[2 * j], v[2 * j + 1]), magic2);   // exact float(P)
+              acc[c32 * 16 + j] = f2_fma(p2, ws2, acc[c32 * 16 + j]);
             }
+            if (a.partials != nullptr && valid) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const int col = wg * kEpiCols + c32 * 32 + j;
+                if (col < tile.rows)
+                  a.partials[(static_cast<int64_t>(tile.m0 + col) * a.N + n) * G + g] =
+                      static_cast<int>(v[j] - kMagicBits);
+              }
+            }
+            __syncwarp();
+            tmem_st_x32_fill(taddr + c32 * 32, kMagicBits);   // re-seed for the next group
           }
         }
+        tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tmem_empty[buf]);
@@ -303,13 +413,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
       }
       if (valid) {
 #pragma unroll
-        for (int c = 0; c < kEpiCols; ++c) {
-          const int col = wg * kEpiCols + c;
+        for (int c = 0; c < kEpiCols / 2; ++c) {
+          const int col = wg * kEpiCols + 2 * c;
           if (col < tile.rows) {
             const int m = tile.m0 + col;
-            const float y = acc[c] * __ldg(a.x_scale + m);
-            a.out[static_cast<int64_t>(m) * a.out_stride0 + static_cast<int64_t>(n) * a.out_stride1] =
-                __float2bfloat16_rn(y);
+            const float lo = __uint_as_float(static_cast<uint32_t>(acc[c]));
+            const float hi = __uint_as_float(static_cast<uint32_t>(acc[c] >> 32));
+            __nv_bfloat16* o = a.out + static_cast<int64_t>(m) * a.out_stride0 + static_cast<int64_t>(n) * a.out_stride1;
+            *o = __float2bfloat16_rn(lo * __ldg(a.x_scale + m));
+            if (col + 1 < tile.rows) o[a.out_stride0] = __float2bfloat16_rn(hi * __ldg(a.x_scale + m + 1));
           }
         }
       }
@@ -357,7 +469,8 @@ bool encode_2d_u8(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t ou
 
 cudaError_t launch_gemm_tc(const GemmArgs& a, cudaStream_t stream) {
   if (a.M_total <= 0) return cudaSuccess;
-  if (a.K < kBK || (a.K % 64) != 0 || (a.gs != 64 && a.gs != 128)) return cudaErrorInvalidValue;
+  if (a.K < kBK || (a.K % 64) != 0 || (a.gs != 64 && a.gs != 128) || a.E > kMaxExperts)
+    return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(a.x_q) & 15) || (a.x_stride0 % 16) ||
       (reinterpret_cast<uintptr_t>(a.w_packed) & 15))
     return cudaErrorInvalidValue;
@@ -367,9 +480,20 @@ cudaError_t launch_gemm_tc(const GemmArgs& a, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   if (!encode_2d_u8(&tm_w, a.w_packed, static_cast<uint64_t>(a.K / 2),
                     static_cast<uint64_t>(a.E) * static_cast<uint64_t>(a.N), static_cast<uint64_t>(a.K / 2),
-                    kBK / 2, kBW, CU_TENSOR_MAP_SWIZZLE_NONE))
+                    kBK / 2, kBW, CU_TENSOR_MAP_SWIZZLE_64B))
     return cudaErrorInvalidValue;
 
+  // The setmaxnreg split (2 x 128 threads at 56 + 2 x 128 at 200 registers)
+  // needs exactly the launch's 512 x 128 registers; with fewer, the
+  // epilogue's setmaxnreg.inc would wait forever, so refuse to launch.
+  static int regs_checked = 0;
+  if (!regs_checked) {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, gemm_tc_kernel);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != 128) return cudaErrorInvalidConfiguration;
+    regs_checked = 1;
+  }
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -380,5 +504,7 @@ cudaError_t launch_gemm_tc(const GemmArgs& a, cudaStream_t stream) {
   gemm_tc_kernel<<<sms, kThreads, smem, stream>>>(tm_x, tm_w, a);
   return cudaGetLastError();
 }
+
+bool gemm_tc_supports(int K, int gs, int E) { return K >= kBK && K % 64 == 0 && (gs == 64 || gs == 128) && E <= kMaxExperts; }
 
 }  // namespace w4a8

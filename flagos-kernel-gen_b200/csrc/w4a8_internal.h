@@ -26,6 +26,7 @@ struct GemmArgs {
 
 cudaError_t launch_gemm_simt(const GemmArgs& a, cudaStream_t stream);
 cudaError_t launch_gemm_tc(const GemmArgs& a, cudaStream_t stream);
+bool gemm_tc_supports(int K, int gs, int E);
 
 int* device_status_ptr();  // per-device status word (static __device__ storage)
 

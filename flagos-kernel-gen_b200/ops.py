@@ -240,6 +240,28 @@ def moe_combine(y: torch.Tensor, inv_pos: torch.Tensor, topk_weights: torch.Tens
     return out
 
 
+def gather_rows(src: torch.Tensor, index: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[i] = src[index[i]] for a 1-D or 2-D tensor (rows with index < 0 untouched)."""
+    dev = _require_cuda(src, index)
+    if index.dtype != torch.int32:
+        raise TypeError("index must be int32")
+    index = index.contiguous()
+    s2 = src if src.dim() == 2 else src.view(-1, 1)
+    if s2.stride(1) != 1:
+        s2 = s2.contiguous()
+    rows = index.numel()
+    if out is None:
+        out = torch.empty((rows,) + tuple(src.shape[1:]), dtype=src.dtype, device=dev)
+    o2 = out if out.dim() == 2 else out.view(-1, 1)
+    if o2.stride(1) != 1 or o2.dtype != src.dtype or o2.shape[1] != s2.shape[1]:
+        raise ValueError("out must match src's row layout")
+    es = src.element_size()
+    rc = _lib.load().w4a8_gather_rows(s2.data_ptr(), s2.stride(0) * es, index.data_ptr(), rows, s2.shape[1] * es,
+                                      o2.data_ptr(), o2.stride(0) * es, _stream(dev))
+    _lib.check(rc, "gather_rows")
+    return out
+
+
 def device_status(reset: bool = True, device: torch.device | None = None) -> int:
     """Reads (and clears) the device status word; synchronises the current stream."""
     dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())

@@ -30,7 +30,7 @@ extern "C" {
 
 /* Kernel selector for w4a8_group_gemm_moe_ex. */
 #define W4A8_KERNEL_AUTO 0 /* tensor-core kernel where its shape rules hold, else CUDA cores */
-#define W4A8_KERNEL_TC 1   /* TMA + tcgen05.mma.kind::i8 kernel (K >= 128, 16-byte aligned x_q rows) */
+#define W4A8_KERNEL_TC 1   /* TMA + tcgen05.mma.kind::i8 kernel (K >= 128, E <= 1024, 16-byte aligned x_q rows) */
 #define W4A8_KERNEL_SIMT 2 /* dp4a CUDA-core kernel (any shape; 4-byte aligned x_q rows) */
 
 int w4a8_abi_version(void);
@@ -134,6 +134,15 @@ int w4a8_silu_mul_requant(const void* h, int64_t h_stride0, int64_t R, int64_t I
 int w4a8_moe_combine(const void* y, int64_t y_stride0, const int32_t* inv_pos, const float* topk_w,
                      int64_t T, int64_t topk, int64_t H, void* out, int64_t out_stride0,
                      void* stream);
+
+/*
+ * Row permutation: dst row i = src row index[i] (row_bytes bytes per row;
+ * strides in bytes; rows with index[i] < 0 are left untouched).  Used by the
+ * expert-parallel path to move received token rows into local expert order
+ * and back.  No reference counterpart.
+ */
+int w4a8_gather_rows(const void* src, int64_t src_stride_bytes, const int32_t* index, int64_t rows,
+                     int64_t row_bytes, void* dst, int64_t dst_stride_bytes, void* stream);
 
 /*
  * Reads (and, if reset != 0, clears) the device status word that the kernels
