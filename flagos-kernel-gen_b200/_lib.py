@@ -21,6 +21,7 @@ W4A8_ERR_DEVICE = 3
 KERNEL_AUTO = 0
 KERNEL_TC = 1
 KERNEL_SIMT = 2
+KERNEL_GEMV = 3
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64

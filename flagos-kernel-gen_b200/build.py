@@ -26,6 +26,7 @@ SOURCES = [
     "ffn_glue.cu",
     "gemm_simt.cu",
     "gemm_tc.cu",
+    "gemm_gemv.cu",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

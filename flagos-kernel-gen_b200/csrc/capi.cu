@@ -109,7 +109,8 @@ int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_
   if (w_q4_packed == nullptr || w_scale == nullptr || w_zero == nullptr || expert_offsets == nullptr)
     return fail(W4A8_ERR_INVALID, "null weight / offset pointer");
   if (x_stride0 < K) return fail(W4A8_ERR_INVALID, "x_q row stride %lld < K", (long long)x_stride0);
-  if (kernel != W4A8_KERNEL_AUTO && kernel != W4A8_KERNEL_TC && kernel != W4A8_KERNEL_SIMT)
+  if (kernel != W4A8_KERNEL_AUTO && kernel != W4A8_KERNEL_TC && kernel != W4A8_KERNEL_SIMT &&
+      kernel != W4A8_KERNEL_GEMV)
     return fail(W4A8_ERR_INVALID, "unknown kernel selector %d", kernel);
   if (M_total == 0) return W4A8_OK;
 
@@ -133,23 +134,50 @@ int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_
   a.K = static_cast<int>(K);
   a.gs = static_cast<int>(group_size);
 
-  const bool tc_ok = gemm_tc_supports((int)K, (int)group_size, (int)E) && (reinterpret_cast<uintptr_t>(x_q) % 16 == 0) && (x_stride0 % 16 == 0) &&
-                     (reinterpret_cast<uintptr_t>(w_q4_packed) % 16 == 0);
+  const bool aligned16 = (reinterpret_cast<uintptr_t>(x_q) % 16 == 0) && (x_stride0 % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(w_q4_packed) % 16 == 0);
+  const bool tc_ok = gemm_tc_supports((int)K, (int)group_size, (int)E) && aligned16;
+  const bool gemv_ok = aligned16;
   const bool simt_ok = (reinterpret_cast<uintptr_t>(x_q) % 4 == 0) && (x_stride0 % 4 == 0);
-  int use = kernel;
-  if (use == W4A8_KERNEL_AUTO) use = tc_ok ? W4A8_KERNEL_TC : W4A8_KERNEL_SIMT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e;
-  if (use == W4A8_KERNEL_TC) {
-    if (!tc_ok)
-      return fail(W4A8_ERR_INVALID,
-                  "tensor-core kernel needs K >= 128, E <= 1024 and 16-byte aligned x_q rows / weights");
-    e = launch_gemm_tc(a, st);
-  } else if (use == W4A8_KERNEL_SIMT) {
-    if (!simt_ok) return fail(W4A8_ERR_INVALID, "CUDA-core kernel needs 4-byte aligned x_q rows");
-    e = launch_gemm_simt(a, st);
-  } else {
-    return fail(W4A8_ERR_INVALID, "unknown kernel selector %d", kernel);
+  cudaError_t e = cudaSuccess;
+  switch (kernel) {
+    case W4A8_KERNEL_TC:
+      if (!tc_ok)
+        return fail(W4A8_ERR_INVALID,
+                    "tensor-core kernel needs K >= 128, E <= 1024 and 16-byte aligned x_q rows / weights");
+      e = launch_gemm_tc(a, st);
+      break;
+    case W4A8_KERNEL_GEMV:
+      if (!gemv_ok) return fail(W4A8_ERR_INVALID, "streaming kernel needs 16-byte aligned x_q rows / weights");
+      e = launch_gemm_gemv(a, st);
+      break;
+    case W4A8_KERNEL_SIMT:
+      if (!simt_ok) return fail(W4A8_ERR_INVALID, "CUDA-core kernel needs 4-byte aligned x_q rows");
+      e = launch_gemm_simt(a, st);
+      break;
+    default: {  // W4A8_KERNEL_AUTO
+      // Experts with at most kGemvMaxTokens rows are weight-streaming bound and
+      // go to the streaming kernel, the others to the tensor-core kernel.  The
+      // split is applied on the device by each kernel's scheduler (row-count
+      // window), so no host synchronisation is needed; a launch whose window
+      // holds no expert exits after its prologue.
+      if (!tc_ok) {
+        if (gemv_ok && M_total <= kGemvMaxTokens) e = launch_gemm_gemv(a, st);
+        else if (simt_ok) e = launch_gemm_simt(a, st);
+        else return fail(W4A8_ERR_INVALID, "x_q rows must be at least 4-byte aligned");
+      } else if (M_total <= kGemvMaxTokens) {
+        e = launch_gemm_gemv(a, st);
+      } else if (M_total >= 64 * E) {
+        e = launch_gemm_tc(a, st);
+      } else {
+        GemmArgs small = a, big = a;
+        small.max_rows = kGemvMaxTokens;
+        big.min_rows = kGemvMaxTokens + 1;
+        e = launch_gemm_gemv(small, st);
+        if (e == cudaSuccess) e = launch_gemm_tc(big, st);
+      }
+    }
   }
   if (e != cudaSuccess) return cuda_fail(e, "grouped GEMM launch");
   return W4A8_OK;

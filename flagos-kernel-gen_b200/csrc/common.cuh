@@ -97,6 +97,35 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   return true;
 }
 
+// Non-suspending probe and a bounded spin on it.  Used by the single thread
+// that issues MMAs: a suspended waiter takes ~250 cycles to wake after the
+// phase completes, which would sit directly on the tensor-core critical path.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, int* status, int code,
+                                          volatile int* abort_flag) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_test_wait(bar, parity)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > W4A8_WAIT_LIMIT_CYCLES) {
+      atomicCAS(status, 0, code);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
 // ----------------------------------------------------------------------------
 // TMA (tiled, 2-D, no multicast)
 // ----------------------------------------------------------------------------
@@ -220,6 +249,8 @@ struct TileSched {
   int* seg;     // [E+1] clamped segment starts; seg[E] unused (smem)
   int* cnt;     // [E] rows per expert (smem)
   int E, bt, NB;
+  int min_rows = 1;           // experts with fewer rows are left to another kernel
+  int max_rows = 0x7fffffff;  // experts with more rows are left to another kernel
 };
 
 // Must be called by all threads of the CTA (contains __syncthreads()).
@@ -230,7 +261,8 @@ __device__ __forceinline__ int sched_build(TileSched& s, const int32_t* __restri
     int a = offsets[e], b = offsets[e + 1];
     a = a < 0 ? 0 : (a > M_total ? M_total : a);
     b = b < 0 ? 0 : (b > M_total ? M_total : b);
-    const int c = b > a ? b - a : 0;
+    int c = b > a ? b - a : 0;
+    if (c < s.min_rows || c > s.max_rows) c = 0;  // not this kernel's expert
     s.seg[e] = a;
     s.cnt[e] = c;
   }

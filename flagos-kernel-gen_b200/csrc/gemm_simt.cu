@@ -35,7 +35,7 @@ gemm_simt_kernel(GemmArgs a) {
   const int wstride = a.gs + 4;
   int8_t* s_w = s_x + kSimtBM * a.gs;
 
-  TileSched s{s_prefix, s_seg, s_cnt, a.E, kSimtBM, (a.N + kSimtBN - 1) / kSimtBN};
+  TileSched s{s_prefix, s_seg, s_cnt, a.E, kSimtBM, (a.N + kSimtBN - 1) / kSimtBN, a.min_rows, a.max_rows};
   const int total = sched_build(s, a.offsets, a.M_total);
   const int G = a.K / a.gs;
   const int tid = threadIdx.x;

@@ -176,7 +176,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   }
 
   TileSched sch{sched_mem, sched_mem + (a.E + 1), sched_mem + 2 * (a.E + 1), a.E, kBT,
-                (a.N + kBW - 1) / kBW};
+                (a.N + kBW - 1) / kBW, a.min_rows, a.max_rows};
   const int total = sched_build(sch, a.offsets, a.M_total);  // contains __syncthreads
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
@@ -259,11 +259,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         for (int g = 0; g < G; ++g) {
           const int sub = g % gpk;
           if (sub == 0) {
-            if (!mbar_wait(&x_full[stage], phase, a.status, kDevTimeoutLoadFull, abort_flag)) goto mma_done;
-            if (!mbar_wait(&a_full[astage], aphase, a.status, kDevTimeoutAFull, abort_flag)) goto mma_done;
+            if (!mbar_spin(&x_full[stage], phase, a.status, kDevTimeoutLoadFull, abort_flag)) goto mma_done;
+            if (!mbar_spin(&a_full[astage], aphase, a.status, kDevTimeoutAFull, abort_flag)) goto mma_done;
             tc_fence_after();
           }
-          if (!mbar_wait(&tmem_empty[buf], bphase ^ 1, a.status, kDevTimeoutTmemEmpty, abort_flag))
+          if (!mbar_spin(&tmem_empty[buf], bphase ^ 1, a.status, kDevTimeoutTmemEmpty, abort_flag))
             goto mma_done;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kBT);
@@ -379,6 +379,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         tc_fence_after();
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                static_cast<uint32_t>(buf * kBT + wg * kEpiCols);
+        // Drain the accumulator: all loads first (a load queued behind a
+        // TMEM store would wait for it), then re-seed the drained columns
+        // with the magic bits in one batch of stores.
 #pragma unroll
         for (int c32 = 0; c32 < kEpiCols / 32; ++c32) {
           if (c32 * 32 < my_cols) {   // warp-uniform
@@ -400,10 +403,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                       static_cast<int>(v[j] - kMagicBits);
               }
             }
-            __syncwarp();
-            tmem_st_x32_fill(taddr + c32 * 32, kMagicBits);   // re-seed for the next group
           }
         }
+        __syncwarp();
+#pragma unroll
+        for (int c32 = 0; c32 < kEpiCols / 32; ++c32)
+          if (c32 * 32 < my_cols) tmem_st_x32_fill(taddr + c32 * 32, kMagicBits);   // re-seed
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();

@@ -22,9 +22,15 @@ struct GemmArgs {
   int* status;                // device status word
   int64_t x_stride0, out_stride0, out_stride1;
   int M_total, E, N, K, gs;
+  // expert row-count window this launch handles (the others are left to the
+  // other kernel of a split launch); default: every expert
+  int min_rows = 1;
+  int max_rows = 0x7fffffff;
 };
 
 cudaError_t launch_gemm_simt(const GemmArgs& a, cudaStream_t stream);
+cudaError_t launch_gemm_gemv(const GemmArgs& a, cudaStream_t stream);
+constexpr int kGemvMaxTokens = 4;  // tokens per pass of the streaming kernel
 cudaError_t launch_gemm_tc(const GemmArgs& a, cudaStream_t stream);
 bool gemm_tc_supports(int K, int gs, int E);
 

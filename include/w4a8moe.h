@@ -29,9 +29,12 @@ extern "C" {
 #define W4A8_ERR_DEVICE 3  /* a kernel reported an error in the device status word */
 
 /* Kernel selector for w4a8_group_gemm_moe_ex. */
-#define W4A8_KERNEL_AUTO 0 /* tensor-core kernel where its shape rules hold, else CUDA cores */
+#define W4A8_KERNEL_AUTO 0 /* experts with <= 4 rows: streaming kernel; others: tensor-core kernel
+                              (CUDA-core kernel where the tensor-core shape rules fail) */
 #define W4A8_KERNEL_TC 1   /* TMA + tcgen05.mma.kind::i8 kernel (K >= 128, E <= 1024, 16-byte aligned x_q rows) */
-#define W4A8_KERNEL_SIMT 2 /* dp4a CUDA-core kernel (any shape; 4-byte aligned x_q rows) */
+#define W4A8_KERNEL_SIMT 2 /* dp4a CUDA-core tile kernel (any shape; 4-byte aligned x_q rows) */
+#define W4A8_KERNEL_GEMV 3 /* weight-streaming CUDA-core kernel for few rows per expert
+                              (16-byte aligned x_q rows / weights) */
 
 int w4a8_abi_version(void);
 const char* w4a8_last_error(void);
