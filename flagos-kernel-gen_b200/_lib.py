@@ -43,6 +43,7 @@ SIGNATURES = {
     "w4a8_silu_mul_requant": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _p, _p]),
     "w4a8_moe_combine": (ctypes.c_int, [_p, _i64, _p, _p, _i64, _i64, _i64, _p, _i64, _p]),
     "w4a8_gather_rows": (ctypes.c_int, [_p, _i64, _p, _i64, _i64, _p, _i64, _p]),
+    "w4a8_moe_align_noalloc": (ctypes.c_int, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p]),
     "w4a8_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32), _i32, _p]),
 }
 

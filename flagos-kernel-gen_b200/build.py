@@ -27,6 +27,7 @@ SOURCES = [
     "gemm_simt.cu",
     "gemm_tc.cu",
     "gemm_gemv.cu",
+    "noalloc.cu",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -66,6 +66,8 @@ cudaError_t bind_stream_device(void* stream) {
 }
 }  // namespace
 
+void set_last_error(const char* msg) { g_last_error = msg; }
+
 int* device_status_ptr() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;

@@ -148,6 +148,23 @@ int w4a8_gather_rows(const void* src, int64_t src_stride_bytes, const int32_t* i
                      int64_t row_bytes, void* dst, int64_t dst_stride_bytes, void* stream);
 
 /*
+ * w4a8_moe_align without a caller workspace, for callers that cannot
+ * allocate device memory (a server whose pool already owns all free device
+ * memory and lends none, or a plain C caller with no allocator).  No
+ * counterpart in the reference.  Same outputs as w4a8_moe_align (bit for
+ * bit); its scratch is a fixed 660 KB array in the library's device memory,
+ * held by every GPU that loads the library until the process exits.
+ * Limits: T*topk <= 131072 and E <= 512, else W4A8_ERR_INVALID with a message.
+ * Allocates nothing.  All calls share the array: calls that overlap on the GPU
+ * race, so serialise them.  The first call on a device resolves the array's
+ * device address; make it before capturing a stream.
+ */
+int w4a8_moe_align_noalloc(const int32_t* topk_ids, int64_t T, int64_t topk, int64_t E,
+                           int64_t block_size, int32_t* expert_offsets, int32_t* sorted_ids,
+                           int32_t* inv_pos, int32_t* padded_ids, int32_t* block_expert,
+                           int32_t* num_post_pad, void* stream);
+
+/*
  * Reads (and, if reset != 0, clears) the device status word that the kernels
  * set when a bounded wait expires.  Synchronises `stream`.  0 = healthy.
  */
