@@ -361,7 +361,7 @@ def main():
     x_h = x.cpu().pin_memory()
     ids_h = ids.cpu().pin_memory()
     tw_h = tw.cpu().pin_memory()
-    out_h = torch.empty((T, layer.out.shape[1]), dtype=torch.bfloat16).pin_memory()
+    out_h = torch.empty((T, cfg.hidden if cfg.ffn else cfg.inter), dtype=torch.bfloat16).pin_memory()
     xd, idsd, twd = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(tw)
 
     def e2e_step():
