@@ -77,17 +77,22 @@ __device__ __forceinline__ uint32_t pack_fold(uint32_t nib4, uint32_t c7, uint32
   return (nib4 + c7) ^ c8;
 }
 
-__device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, uint32_t (&r)[32]) {
+// 32 lanes x 32 columns, followed by the wait in the same asm statement: the
+// destination registers are only written when the asynchronous load lands, so
+// the compiler must not see them as defined before the wait.
+__device__ __forceinline__ void tmem_ld_x32_wait(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
         "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
         "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
         "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
+      : "r"(taddr)
+      : "memory");
 }
 
 // Store the same 32-bit value to 32 consecutive columns of this warp's lanes.
@@ -387,8 +392,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
           if (c32 * 32 < my_cols) {   // warp-uniform
             uint32_t v[32];
             __syncwarp();
-            tmem_ld_x32(taddr + c32 * 32, v);
-            tmem_ld_wait();
+            tmem_ld_x32_wait(taddr + c32 * 32, v);
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const uint64_t p2 = f2_sub(u2_pack(v[2 * j], v[2 * j + 1]), magic2);   // exact float(P)
