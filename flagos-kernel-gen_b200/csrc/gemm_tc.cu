@@ -13,13 +13,14 @@
 // the M side every epilogue thread owns one output channel, so the per-group
 // weight scale is one register per thread.
 //
-// Exact int32 -> fp32 without I2F: before a group's first MMA each TMEM
-// accumulator holds the bit pattern of 1.5 * 2^23 (0x4B400000).  The MMAs add
-// the integer partial P to those bits; for |P| < 2^22 (|P| <= 2^21 here) the
-// result, read as fp32, is exactly 1.5 * 2^23 + P, so one exact FADD recovers
-// float(P).  Scale accumulation then uses packed fp32x2 FADD/FFMA, which round
-// exactly like the scalar fmaf of the CUDA-core kernel (both kernels produce
-// identical bits).
+// Per K-group accumulators: the first MMA of a group overwrites its TMEM
+// accumulator (enable-input-d off), the rest accumulate, so TMEM holds the
+// exact int32 partial P.  Exact int32 -> fp32 without I2F: the epilogue adds
+// the bit pattern of 1.5 * 2^23 (0x4B400000) to P; for |P| < 2^22 (|P| <= 2^21
+// here) the sum read as fp32 is exactly 1.5 * 2^23 + P, and one exact FSUB
+// recovers float(P).  Scale accumulation then uses packed fp32x2 FSUB/FFMA,
+// which round exactly like the scalar fmaf of the CUDA-core kernel (both
+// kernels produce identical bits).
 //
 // Warp roles (512 threads, one CTA per SM, persistent over tiles):
 //   warp 0      TMA producer of token tiles [rows x 128 B] (128-byte swizzle)
@@ -29,7 +30,15 @@
 //   warps 4-7   transform: thread r unpacks weight row r (nibble order of
 //               docs/Task1.md:78-81, zero fold with the int8 wrap of :84-85)
 //               into the canonical 128B-swizzled K-major layout the MMA reads
-//   warps 8-15  epilogue: two warpgroups of 128 token columns each
+//   warps 8-15  epilogue: two warpgroups of 128 token columns each; an
+//               accumulator is handed back to the MMA as soon as its last
+//               columns are in registers, before their fp32 math
+//
+// The packed-weight ring is read with ordinary shared loads and refilled by
+// TMA (async proxy): a stage is released only after the unpacked bytes that
+// depend on every loaded value have been stored, so no refill can overtake
+// an outstanding read.
+//
 // Register split (setmaxnreg): warpgroups 0-1 drop to 56, the epilogue
 // warpgroups rise to 200: 2*128*56 + 2*128*200 = 65536 = the launch's 512 x 128.
 #include "common.cuh"
@@ -93,19 +102,6 @@ __device__ __forceinline__ void tmem_ld_x32_wait(uint32_t taddr, uint32_t (&r)[3
         "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr)
       : "memory");
-}
-
-// Store the same 32-bit value to 32 consecutive columns of this warp's lanes.
-__device__ __forceinline__ void tmem_st_x32_fill(uint32_t taddr, uint32_t v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
-      "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-      "r"(v)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_st_wait() {
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
@@ -186,21 +182,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  // Epilogue warps seed both accumulators with the magic bits before any MMA.
-  if (warp >= kEpilogueWarp0) {
-    const int quarter = warp & 3;
-    const int wg = (warp - kEpilogueWarp0) >> 2;
-    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-#pragma unroll
-    for (int b = 0; b < 2; ++b)
-#pragma unroll
-      for (int c = 0; c < kEpiCols / 32; ++c)
-        tmem_st_x32_fill(lane_base + b * kBT + wg * kEpiCols + c * 32, kMagicBits);
-    tmem_st_wait();
-    tc_fence_before();
-  }
-  __syncthreads();
-  tc_fence_after();
 
   const int G = a.K / a.gs;
   const int KB = (a.K + kBK - 1) / kBK;
@@ -255,34 +236,34 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
+      const uint64_t desc_x0 = make_desc_sw128(smem_u32(sX));
+      const uint64_t desc_a0 = make_desc_sw128(smem_u32(sA));
       int stage = 0, astage = 0, buf = 0;
       uint32_t phase = 0, aphase = 0, bphase = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         const Tile tile = sched_tile(sch, t);
         const int n_mma = (tile.rows + 15) & ~15;
         const uint32_t idesc = make_idesc_i8(kBW, n_mma);
+        int sub = 0;   // group within the K block (gs = 64: two groups per block)
         for (int g = 0; g < G; ++g) {
-          const int sub = g % gpk;
           if (sub == 0) {
-            if (!mbar_spin(&x_full[stage], phase, a.status, kDevTimeoutLoadFull, abort_flag)) goto mma_done;
-            if (!mbar_spin(&a_full[astage], aphase, a.status, kDevTimeoutAFull, abort_flag)) goto mma_done;
-            tc_fence_after();
+            if (!mbar_wait(&x_full[stage], phase, a.status, kDevTimeoutLoadFull, abort_flag)) goto mma_done;
+            if (!mbar_wait(&a_full[astage], aphase, a.status, kDevTimeoutAFull, abort_flag)) goto mma_done;
           }
-          if (!mbar_spin(&tmem_empty[buf], bphase ^ 1, a.status, kDevTimeoutTmemEmpty, abort_flag))
+          if (!mbar_wait(&tmem_empty[buf], bphase ^ 1, a.status, kDevTimeoutTmemEmpty, abort_flag))
             goto mma_done;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kBT);
-          const uint32_t a_addr = smem_u32(sA + astage * kABytes);
-          const uint32_t b_addr = smem_u32(sX + stage * kXBytes);
-          for (int ks = 0; ks < kpg; ++ks) {
-            const uint32_t koff = static_cast<uint32_t>((sub * kpg + ks) * 32);
-            // always accumulate: the accumulator starts from the magic bits
-            mma_i8_ss(d_tmem, make_desc_sw128(a_addr + koff), make_desc_sw128(b_addr + koff), idesc, 1u);
-          }
+          // descriptors advance by (byte offset >> 4) in their start-address field
+          const uint64_t adesc = desc_a0 + static_cast<uint64_t>((astage * kABytes + sub * kpg * 32) >> 4);
+          const uint64_t bdesc = desc_x0 + static_cast<uint64_t>((stage * kXBytes + sub * kpg * 32) >> 4);
+          for (int ks = 0; ks < kpg; ++ks)   // the group's first K step overwrites the accumulator
+            mma_i8_ss(d_tmem, adesc + 2 * ks, bdesc + 2 * ks, idesc, ks > 0 ? 1u : 0u);
           mma_commit(&tmem_full[buf]);
           buf ^= 1;
           if (buf == 0) bphase ^= 1;
-          if (sub == gpk - 1 || g == G - 1) {
+          if (++sub == gpk || g == G - 1) {
+            sub = 0;
             mma_commit(&x_empty[stage]);
             mma_commit(&a_empty[astage]);
             if (++stage == kXStages) { stage = 0; phase ^= 1; }
@@ -323,8 +304,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
 #pragma unroll
           for (int c = 0; c < 4; ++c) pk[c] = *reinterpret_cast<const uint4*>(src + ((c ^ sw) << 4));
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&w_empty[stage]);
+        // The packed stage is released only after its bytes have been consumed
+        // (below): the release is a generic-proxy arrive while the refill is an
+        // async-proxy TMA write, so an arrive issued right after the shared
+        // loads does not order them before the refill.
+        const int wstage = stage;
         if (++stage == kWStages) { stage = 0; phase ^= 1; }
 
         if (!mbar_wait(&a_empty[astage], aphase ^ 1, a.status, kDevTimeoutAEmpty, abort_flag)) goto tr_done;
@@ -351,7 +335,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[astage]);
+        if (lane == 0) {
+          mbar_arrive(&w_empty[wstage]);   // the stores above depend on every byte read from it
+          mbar_arrive(&a_full[astage]);
+        }
         if (++astage == kAStages) { astage = 0; aphase ^= 1; }
       }
     }
@@ -384,18 +371,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         tc_fence_after();
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                static_cast<uint32_t>(buf * kBT + wg * kEpiCols);
-        // Drain the accumulator: all loads first (a load queued behind a
-        // TMEM store would wait for it), then re-seed the drained columns
-        // with the magic bits in one batch of stores.
+        // Drain 32 columns per load; the accumulator goes back to the MMA as
+        // soon as the last chunk is in registers, before its math.
 #pragma unroll
         for (int c32 = 0; c32 < kEpiCols / 32; ++c32) {
-          if (c32 * 32 < my_cols) {   // warp-uniform
-            uint32_t v[32];
+          const bool have = c32 * 32 < my_cols;   // warp-uniform
+          uint32_t v[32];
+          __syncwarp();
+          if (have) tmem_ld_x32_wait(taddr + c32 * 32, v);
+          if (c32 == kEpiCols / 32 - 1) {
+            tc_fence_before();
             __syncwarp();
-            tmem_ld_x32_wait(taddr + c32 * 32, v);
+            if (lane == 0) mbar_arrive(&tmem_empty[buf]);
+          }
+          if (have) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const uint64_t p2 = f2_sub(u2_pack(v[2 * j], v[2 * j + 1]), magic2);   // exact float(P)
+            for (int j = 0; j < 16; ++j) {   // P + 1.5 * 2^23 read as fp32, minus 1.5 * 2^23 = float(P)
+              const uint64_t p2 = f2_sub(u2_pack(v[2 * j] + kMagicBits, v[2 * j + 1] + kMagicBits), magic2);
               acc[c32 * 16 + j] = f2_fma(p2, ws2, acc[c32 * 16 + j]);
             }
             if (a.partials != nullptr && valid) {
@@ -403,20 +395,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
               for (int j = 0; j < 32; ++j) {
                 const int col = wg * kEpiCols + c32 * 32 + j;
                 if (col < tile.rows)
-                  a.partials[(static_cast<int64_t>(tile.m0 + col) * a.N + n) * G + g] =
-                      static_cast<int>(v[j] - kMagicBits);
+                  a.partials[(static_cast<int64_t>(tile.m0 + col) * a.N + n) * G + g] = static_cast<int>(v[j]);
               }
             }
           }
         }
-        __syncwarp();
-#pragma unroll
-        for (int c32 = 0; c32 < kEpiCols / 32; ++c32)
-          if (c32 * 32 < my_cols) tmem_st_x32_fill(taddr + c32 * 32, kMagicBits);   // re-seed
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tmem_empty[buf]);
         buf ^= 1;
         if (buf == 0) bphase ^= 1;
       }
