@@ -2,23 +2,33 @@
 // are read from HBM exactly once by the TMA engine, CUDA cores do the math.
 //
 // At 1-4 tokens per expert the layer is bound by reading the packed weights.
-// A 128-row tensor-core tile with N = 16 pays a fixed ~64-cycle MMA floor per
-// 32-byte K step plus TMEM round trips per K-group, longer than its 8 KB of
-// weights take to arrive, so this path keeps the tensor cores out of it:
+// A 128-row tensor-core tile with N = 16 pays a fixed per-group cost (MMA
+// issue, TMEM round trip, barrier hand-offs) longer than its 8 KB of weights
+// take to arrive, so this path keeps the tensor cores out of it:
 //   * one producer warp streams a block of RB contiguous weight rows of one
-//     expert (RB * K/2 bytes, <= 32 KB) into a 4-stage shared-memory ring with
-//     a single cp.async.bulk per stage (no multicast), plus the block's
+//     expert (RB * K/2 bytes, about 32 KB) into a shared-memory ring with a
+//     single cp.async.bulk per stage (no multicast), plus the block's
 //     w_scale / w_zero rows (bulk copies when 16-byte aligned, else loaded by
 //     the consumers directly);
-//   * eight consumer warps each take rows of the block: lanes read 16 packed
-//     bytes (32 K values) per 1024-wide K step from shared memory, unpack the
-//     nibbles and fold the zero point with the reference's int8 wrap
-//     (docs/Task1.md:78-85), dp4a against up to kGvRows token rows (read from
-//     L1: every row of the expert uses them);
+//   * the token rows of the current expert (at most kGvRows) are staged once
+//     in shared memory, split per 8-byte K block into the even-k and odd-k
+//     bytes, i.e. the order in which the low and high nibbles of a packed
+//     word come out of a mask and a shift, together with the sum of every
+//     32-value chunk of each row;
+//   * eight consumer warps each take rows of the block: a lane handles 32 K
+//     values (16 packed bytes) per 1024-wide K step.  The exact int32 partial
+//     of docs/Task1.md:100-104 is
+//         sum_k int8(nib - z) * x  =  sum_k nib * x  -  z * sum_k x
+//     whenever nib - z cannot leave int8 (z >= -112), so the raw nibbles go
+//     straight into dp4a (unsigned x signed; the odd-k nibbles are left in
+//     the high half of their bytes and the 16x sum is shifted back) and the
+//     zero point costs one multiply per chunk;
+//     groups whose zero point can wrap (z < -112) fold each nibble with the
+//     reference's int8 wrap instead (docs/Task1.md:78-85);
 //   * the 4 (gs = 128) or 2 (gs = 64) lanes of a K-group are summed with
-//     shuffles -> the exact int32 partial of docs/Task1.md:100-104; the group's
-//     first lane applies w_scale, a warp reduction and x_scale give the bf16
-//     output (docs/Task1.md:107-112).
+//     shuffles -> the exact int32 partial; the group's first lane applies
+//     w_scale, a warp reduction and x_scale give the bf16 output
+//     (docs/Task1.md:107-112).
 // fp32 summation order differs from the tile kernels (per lane, then across
 // lanes): outputs agree with them within bf16 rounding; int32 partials are
 // identical.
@@ -32,19 +42,22 @@ namespace {
 constexpr int kGvConsumers = 8;
 constexpr int kGvThreads = (kGvConsumers + 1) * 32;   // + producer warp
 constexpr int kGvRows = kGemvMaxTokens;                // tokens per pass
-constexpr int kGvMaxStages = 4;   // ring depth per CTA (two CTAs per SM)
+constexpr int kGvMaxStages = 4;   // ring depth per CTA
 constexpr int kGvTargetW = 32 * 1024;                  // preferred weight bytes per stage
 constexpr int kGvMaxRB = 32;                           // rows per block
-constexpr int kGvSmemBudget = 110 * 1024;   // two CTAs per SM
+constexpr int kGvSmemBudget = 110 * 1024;   // two CTAs per SM when it fits
+constexpr int kWrapZero = -112;   // z >= kWrapZero: nib - z stays inside int8 for every nibble
 
 struct GvParams {
-  int stages;      // ring depth (2..4)
+  int stages;      // ring depth (1..4)
   int stage_w;     // weight bytes per stage (RB * row_bytes)
   int RB;          // weight rows per block (a multiple of the consumer warp count)
   int row_bytes;   // K/2
   int meta_bulk;   // 1: scales / zero points travel with the block (16-byte aligned)
   int ws_bytes;    // per-stage bytes reserved for scales (RB*G*4, 16-aligned)
   int z_bytes;     // per-stage bytes reserved for zero points (RB*G, 16-aligned)
+  int x_bytes;     // token tile: kGvRows rows x K bytes (even half + odd half)
+  int sx_bytes;    // chunk sums: kGvRows rows x K/32 int32
 };
 
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
@@ -55,62 +68,108 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
-__device__ __forceinline__ void unpack_fold(uint4 w, int z, uint32_t (&o)[8]) {
-  const uint32_t cb = static_cast<uint32_t>(-z) & 0xFFu;
-  const uint32_t c7 = (cb & 0x7Fu) * 0x01010101u;
-  const uint32_t c8 = (cb & 0x80u) * 0x01010101u;
-  const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint32_t lo = wv[q] & 0x0F0F0F0Fu;
-    const uint32_t hi = (wv[q] >> 4) & 0x0F0F0F0Fu;
-    o[2 * q] = (__byte_perm(lo, hi, 0x5140) + c7) ^ c8;
-    o[2 * q + 1] = (__byte_perm(lo, hi, 0x7362) + c7) ^ c8;
-  }
+// Named barrier over the consumer warps only (the producer keeps streaming).
+__device__ __forceinline__ void consumers_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kGvConsumers * 32) : "memory");
 }
+
+// dp4a with unsigned bytes in a and signed bytes in b.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+struct TokenTile {
+  const uint8_t* xe;   // [kGvRows][K/2] even-k bytes, 16 per 32-value chunk
+  const uint8_t* xo;   // [kGvRows][K/2] odd-k bytes
+  const int* sx;       // [kGvRows][K/32] chunk sums
+};
 
 struct RowJob {
   const uint8_t* w;      // packed weight row in shared memory
   const int8_t* z;       // zero points of the row in shared memory (nullptr: read global)
   const float* ws;       // scales of the row in shared memory (nullptr: read global)
-  const int8_t* x;       // first token row of the tile (global)
   int m0, n;             // first token row, output channel
   int64_t grow;          // e * N + n
 };
 
-// One weight row against R token rows (R = the tile's token count).
+// One weight row against R token rows (R = the tile's token count).  Lane l
+// handles 32-value chunk 32 * s + l of K step s; everything that depends on
+// the step advances by constant strides (no divisions in the loop).
 template <int R>
-__device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, int G, int lane) {
-  const int lpg = a.gs / 32;   // lanes per K-group (4 or 2)
+__device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const TokenTile& tt, int G, int lane,
+                                       int lpg_shift) {
+  const int lpg = 1 << lpg_shift;          // lanes per K-group (4 or 2)
+  const int gstep = 32 >> lpg_shift;       // groups per K step (8 or 16)
+  const int half_k = a.K >> 1;
+  const int nchunk = a.K >> 5;
+  const bool leader = (lane & (lpg - 1)) == 0;
+  const uint8_t* wp = j.w + 16 * lane;
+  const uint8_t* xep = tt.xe + 16 * lane;
+  const uint8_t* xop = tt.xo + 16 * lane;
+  const int* sxp = tt.sx + lane;
+  int g = lane >> lpg_shift;
+  int c = lane;
   float acc[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) acc[r] = 0.f;
 #pragma unroll 2
   for (int kstep = 0; kstep < a.K; kstep += 1024) {
-    const int k0 = kstep + lane * 32;
-    const bool active = k0 < a.K;
-    const int g = active ? k0 / a.gs : 0;
+    const bool active = c < nchunk;
     int p[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) p[r] = 0;
     if (active) {
       const int z = j.z != nullptr ? j.z[g] : a.w_zero[j.grow * G + g];
-      uint32_t o[8];
-      unpack_fold(*reinterpret_cast<const uint4*>(j.w + k0 / 2), z, o);
+      const uint4 w = *reinterpret_cast<const uint4*>(wp);
+      const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+      const bool wrap = z < kWrapZero;
+      if (!wrap) {
+        // lo: the even-k nibbles as bytes 0..15; hi16: the odd-k nibbles left
+        // in the high half of each byte (16 * nib, taken as unsigned), so their
+        // dot product is 16x the true one and one arithmetic shift restores it.
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const uint4* xr = reinterpret_cast<const uint4*>(j.x + static_cast<int64_t>(r) * a.x_stride0 + k0);
-        const uint4 x0 = __ldg(xr), x1 = __ldg(xr + 1);
-        int s = 0;
-        s = __dp4a(static_cast<int>(o[0]), static_cast<int>(x0.x), s);
-        s = __dp4a(static_cast<int>(o[1]), static_cast<int>(x0.y), s);
-        s = __dp4a(static_cast<int>(o[2]), static_cast<int>(x0.z), s);
-        s = __dp4a(static_cast<int>(o[3]), static_cast<int>(x0.w), s);
-        s = __dp4a(static_cast<int>(o[4]), static_cast<int>(x1.x), s);
-        s = __dp4a(static_cast<int>(o[5]), static_cast<int>(x1.y), s);
-        s = __dp4a(static_cast<int>(o[6]), static_cast<int>(x1.z), s);
-        s = __dp4a(static_cast<int>(o[7]), static_cast<int>(x1.w), s);
-        p[r] = s;
+        for (int r = 0; r < R; ++r) {
+          const uint4 xe = *reinterpret_cast<const uint4*>(xep + r * half_k);
+          const uint4 xo = *reinterpret_cast<const uint4*>(xop + r * half_k);
+          int se = -z * sxp[r * nchunk], so = 0;
+          se = dp4a_us(wv[0] & 0x0F0F0F0Fu, xe.x, se);
+          so = dp4a_us(wv[0] & 0xF0F0F0F0u, xo.x, so);
+          se = dp4a_us(wv[1] & 0x0F0F0F0Fu, xe.y, se);
+          so = dp4a_us(wv[1] & 0xF0F0F0F0u, xo.y, so);
+          se = dp4a_us(wv[2] & 0x0F0F0F0Fu, xe.z, se);
+          so = dp4a_us(wv[2] & 0xF0F0F0F0u, xo.z, so);
+          se = dp4a_us(wv[3] & 0x0F0F0F0Fu, xe.w, se);
+          so = dp4a_us(wv[3] & 0xF0F0F0F0u, xo.w, so);
+          p[r] = se + (so >> 4);
+        }
+      } else {
+        // byte-wise (nib - z) mod 256: nib + (c & 0x7f) never carries, the top bit is an XOR
+        const uint32_t cb = static_cast<uint32_t>(-z) & 0xFFu;
+        const uint32_t c7 = (cb & 0x7Fu) * 0x01010101u;
+        const uint32_t c8 = (cb & 0x80u) * 0x01010101u;
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          lo[q] = ((wv[q] & 0x0F0F0F0Fu) + c7) ^ c8;            // k = 8q + 0, 2, 4, 6 of the chunk
+          hi[q] = (((wv[q] >> 4) & 0x0F0F0F0Fu) + c7) ^ c8;     // k = 8q + 1, 3, 5, 7
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const uint4 xe = *reinterpret_cast<const uint4*>(xep + r * half_k);
+          const uint4 xo = *reinterpret_cast<const uint4*>(xop + r * half_k);
+          int s = 0;
+          s = __dp4a(static_cast<int>(lo[0]), static_cast<int>(xe.x), s);
+          s = __dp4a(static_cast<int>(hi[0]), static_cast<int>(xo.x), s);
+          s = __dp4a(static_cast<int>(lo[1]), static_cast<int>(xe.y), s);
+          s = __dp4a(static_cast<int>(hi[1]), static_cast<int>(xo.y), s);
+          s = __dp4a(static_cast<int>(lo[2]), static_cast<int>(xe.z), s);
+          s = __dp4a(static_cast<int>(hi[2]), static_cast<int>(xo.z), s);
+          s = __dp4a(static_cast<int>(lo[3]), static_cast<int>(xe.w), s);
+          s = __dp4a(static_cast<int>(hi[3]), static_cast<int>(xo.w), s);
+          p[r] = s;
+        }
       }
     }
 #pragma unroll
@@ -118,7 +177,7 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, int G
       p[r] += __shfl_xor_sync(0xffffffffu, p[r], 1);
       if (lpg == 4) p[r] += __shfl_xor_sync(0xffffffffu, p[r], 2);
     }
-    if (active && (lane % lpg) == 0) {
+    if (active && leader) {
       const float ws = j.ws != nullptr ? j.ws[g] : __ldg(a.w_scale + j.grow * G + g);
 #pragma unroll
       for (int r = 0; r < R; ++r) {
@@ -126,6 +185,12 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, int G
         if (a.partials != nullptr) a.partials[(static_cast<int64_t>(j.m0 + r) * a.N + j.n) * G + g] = p[r];
       }
     }
+    wp += 512;
+    xep += 512;
+    xop += 512;
+    sxp += 32;
+    g += gstep;
+    c += 32;
   }
 #pragma unroll
   for (int r = 0; r < R; ++r) {
@@ -140,12 +205,41 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, int G
   }
 }
 
+// Stages the token rows [m0, m0 + rows) of x_q: per 32-value chunk, the 16
+// even-k bytes, the 16 odd-k bytes and the chunk sum.  Called by all
+// consumer threads between two consumer barriers.
+__device__ __forceinline__ void stage_tokens(const GemmArgs& a, int m0, int rows, uint8_t* xe, uint8_t* xo, int* sx) {
+  const int half_k = a.K >> 1;
+  const int nchunk = a.K >> 5;
+  for (int i = threadIdx.x; i < rows * nchunk; i += kGvConsumers * 32) {
+    const int r = i / nchunk, c = i - r * nchunk;
+    const uint4* src = reinterpret_cast<const uint4*>(a.x_q + static_cast<int64_t>(m0 + r) * a.x_stride0 + 32 * c);
+    const uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
+    const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    uint32_t e[4], o[4];
+    int s = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {   // 8 bytes x0..x7 -> (x0, x2, x4, x6) and (x1, x3, x5, x7)
+      e[q] = __byte_perm(wv[2 * q], wv[2 * q + 1], 0x6420);
+      o[q] = __byte_perm(wv[2 * q], wv[2 * q + 1], 0x7531);
+      s = __dp4a(static_cast<int>(wv[2 * q]), 0x01010101, s);
+      s = __dp4a(static_cast<int>(wv[2 * q + 1]), 0x01010101, s);
+    }
+    *reinterpret_cast<uint4*>(xe + r * half_k + 16 * c) = make_uint4(e[0], e[1], e[2], e[3]);
+    *reinterpret_cast<uint4*>(xo + r * half_k + 16 * c) = make_uint4(o[0], o[1], o[2], o[3]);
+    sx[r * nchunk + c] = s;
+  }
+}
+
 __global__ void __launch_bounds__(kGvThreads, 2)
 gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
   extern __shared__ unsigned char smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int stage_bytes = gp.stage_w + gp.ws_bytes + gp.z_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(base + gp.stages * stage_bytes);
+  uint8_t* s_xe = base + gp.stages * stage_bytes;
+  uint8_t* s_xo = s_xe + gp.x_bytes / 2;
+  int* s_sx = reinterpret_cast<int*>(s_xe + gp.x_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(s_sx) + gp.sx_bytes);
   uint64_t* empty = full + kGvMaxStages;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kGvMaxStages);
   int* sched_mem = const_cast<int*>(reinterpret_cast<volatile int*>(abort_flag)) + 4;
@@ -164,7 +258,7 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
   const int total = sched_build(sch, a.offsets, a.M_total);   // contains __syncthreads
   const int G = a.K / a.gs;
   // Each CTA takes a contiguous range of blocks: consecutive blocks belong to
-  // the same expert, so its token rows stay resident in this SM's L1.
+  // the same expert, so its token rows are staged once for many blocks.
   const int per_cta = (total + gridDim.x - 1) / gridDim.x;
   const int t_begin = min(total, static_cast<int>(blockIdx.x) * per_cta);
   const int t_end = min(total, t_begin + per_cta);
@@ -196,26 +290,41 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
     }
   } else {
     // ------------------------------------------------------------ consumers
+    const TokenTile tt{s_xe, s_xo, s_sx};
+    const int lpg_shift = a.gs == 128 ? 2 : 1;
+    int cur_m0 = -1, cur_rows = 0;
     int stage = 0;
     uint32_t phase = 0;
+    bool failed = false;   // after a timed-out wait, keep walking the tiles (no work) so the
+                           // consumer barriers below still see every consumer warp
     for (int t = t_begin; t < t_end; ++t) {
       const Tile tile = sched_tile(sch, t);
+      if (tile.m0 != cur_m0 || tile.rows != cur_rows) {   // uniform over the consumers
+        consumers_sync();                                 // nobody still reads the old rows
+        stage_tokens(a, tile.m0, tile.rows, s_xe, s_xo, s_sx);
+        consumers_sync();
+        cur_m0 = tile.m0;
+        cur_rows = tile.rows;
+      }
+      if (failed) continue;
       const int n0 = tile.nb * gp.RB;
       const int rows = min(gp.RB, a.N - n0);
-      if (!mbar_wait(&full[stage], phase, a.status, kDevTimeoutLoadFull, abort_flag)) break;
+      if (!mbar_wait(&full[stage], phase, a.status, kDevTimeoutLoadFull, abort_flag)) {
+        failed = true;
+        continue;
+      }
       const uint8_t* st = base + stage * stage_bytes;
       const float* s_ws = reinterpret_cast<const float*>(st + gp.stage_w);
       const int8_t* s_z = reinterpret_cast<const int8_t*>(st + gp.stage_w + gp.ws_bytes);
-      const int8_t* xbase = a.x_q + static_cast<int64_t>(tile.m0) * a.x_stride0;
       for (int rr = warp; rr < rows; rr += kGvConsumers) {
         const RowJob job{st + rr * gp.row_bytes, gp.meta_bulk ? s_z + rr * G : nullptr,
-                         gp.meta_bulk ? s_ws + rr * G : nullptr, xbase, tile.m0, n0 + rr,
+                         gp.meta_bulk ? s_ws + rr * G : nullptr, tile.m0, n0 + rr,
                          static_cast<int64_t>(tile.e) * a.N + n0 + rr};
         switch (tile.rows) {   // warp-uniform: the tile's token count
-          case 1: gv_row<1>(a, job, G, lane); break;
-          case 2: gv_row<2>(a, job, G, lane); break;
-          case 3: gv_row<3>(a, job, G, lane); break;
-          default: gv_row<4>(a, job, G, lane); break;
+          case 1: gv_row<1>(a, job, tt, G, lane, lpg_shift); break;
+          case 2: gv_row<2>(a, job, tt, G, lane, lpg_shift); break;
+          case 3: gv_row<3>(a, job, tt, G, lane, lpg_shift); break;
+          default: gv_row<4>(a, job, tt, G, lane, lpg_shift); break;
         }
       }
       __syncwarp();
@@ -250,10 +359,17 @@ cudaError_t launch_gemm_gemv(const GemmArgs& a, cudaStream_t stream) {
                  (reinterpret_cast<uintptr_t>(a.w_zero) % 16 == 0);
   gp.ws_bytes = gp.meta_bulk ? gp.RB * G * 4 : 0;
   gp.z_bytes = gp.meta_bulk ? ((gp.RB * G + 15) / 16) * 16 : 0;
+  gp.x_bytes = kGvRows * a.K;                    // K is a multiple of 64: both halves stay 16-byte aligned
+  gp.sx_bytes = kGvRows * (a.K / 32) * 4;
   const size_t stage_bytes = gp.stage_w + gp.ws_bytes + gp.z_bytes;
-  const size_t fixed = 128 + 2 * kGvMaxStages * 8 + 16 + sizeof(int) * 3 * (a.E + 1);
+  const size_t fixed = 128 + gp.x_bytes + gp.sx_bytes + 2 * kGvMaxStages * 8 + 16 + sizeof(int) * 3 * (a.E + 1);
+  // deepest ring that keeps two CTAs per SM, else the deepest that fits one
   gp.stages = kGvMaxStages;
   while (gp.stages > 2 && fixed + gp.stages * stage_bytes > kGvSmemBudget) --gp.stages;
+  if (fixed + gp.stages * stage_bytes > kGvSmemBudget) {
+    gp.stages = kGvMaxStages;
+    while (gp.stages > 1 && fixed + gp.stages * stage_bytes > 227 * 1024) --gp.stages;
+  }
   const size_t smem = fixed + gp.stages * stage_bytes;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(gemm_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -217,12 +217,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   } else if (warp == 2) {
     // ------------------------------------------------------------ TMA producer: packed weights
     if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_keep = policy_evict_last(), pol_drop = policy_evict_first();
       int stage = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         const Tile tile = sched_tile(sch, t);
         const int wrow = tile.e * a.N + tile.nb * kBW;
+        // The token blocks of one weight block run as neighbouring tiles: the
+        // earlier ones keep the weight block in L2 for the later ones, the
+        // last one lets it go.
+        const bool last_tb = tile.m0 + tile.rows >= sch.seg[tile.e] + sch.cnt[tile.e];
+        const uint64_t pol_w = last_tb ? pol_drop : pol_keep;
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(&w_empty[stage], phase ^ 1, a.status, kDevTimeoutLoadEmpty, abort_flag))
             goto w_done;
