@@ -57,7 +57,7 @@ struct GvParams {
   int ws_bytes;    // per-stage bytes reserved for scales (RB*G*4, 16-aligned)
   int z_bytes;     // per-stage bytes reserved for zero points (RB*G, 16-aligned)
   int x_bytes;     // token tile: kGvRows rows x K bytes (even half + odd half)
-  int sx_bytes;    // chunk sums: kGvRows rows x K/32 int32
+  int sx_bytes;    // group sums: kGvRows rows x G int32
 };
 
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
@@ -83,7 +83,7 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
 struct TokenTile {
   const uint8_t* xe;   // [kGvRows][K/2] even-k bytes, 16 per 32-value chunk
   const uint8_t* xo;   // [kGvRows][K/2] odd-k bytes
-  const int* sx;       // [kGvRows][K/32] chunk sums
+  const int* sx;       // [kGvRows][G] group sums
 };
 
 struct RowJob {
@@ -95,71 +95,80 @@ struct RowJob {
 };
 
 // One weight row against R token rows (R = the tile's token count).  Lane l
-// handles 32-value chunk 32 * s + l of K step s; everything that depends on
-// the step advances by constant strides (no divisions in the loop).
-template <int R>
-__device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const TokenTile& tt, int G, int lane,
-                                       int lpg_shift) {
-  const int lpg = 1 << lpg_shift;          // lanes per K-group (4 or 2)
-  const int gstep = 32 >> lpg_shift;       // groups per K step (8 or 16)
+// owns K-groups l, l + 32, ...: it reads the group's GS/2 packed bytes as
+// GS/32 16-byte chunks (visited in a lane-rotated order, so the 16-byte
+// shared loads of a quarter warp hit distinct banks), forms the exact int32
+// partial on its own and applies w_scale; one warp reduction per token row
+// finishes the output.
+template <int R, int GS>
+__device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const TokenTile& tt, int G, int lane) {
+  constexpr int kCpg = GS / 32;                 // 16-byte packed chunks per group
+  constexpr int kRot = kCpg == 4 ? 1 : 2;       // lane -> chunk rotation (conflict-free quarter warps)
   const int half_k = a.K >> 1;
-  const int nchunk = a.K >> 5;
-  const bool leader = (lane & (lpg - 1)) == 0;
-  const uint8_t* wp = j.w + 16 * lane;
-  const uint8_t* xep = tt.xe + 16 * lane;
-  const uint8_t* xop = tt.xo + 16 * lane;
-  const int* sxp = tt.sx + lane;
-  int g = lane >> lpg_shift;
-  int c = lane;
+  const int rot = lane >> kRot;
   float acc[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) acc[r] = 0.f;
-#pragma unroll 2
-  for (int kstep = 0; kstep < a.K; kstep += 1024) {
-    const bool active = c < nchunk;
+  for (int g = lane; g < G; g += 32) {
+    const int z = j.z != nullptr ? j.z[g] : a.w_zero[j.grow * G + g];
+    const uint8_t* wg = j.w + g * (GS / 2);
+    const uint8_t* xeg = tt.xe + g * (GS / 2);
+    const uint8_t* xog = tt.xo + g * (GS / 2);
     int p[R];
+    if (z >= kWrapZero) {
+      // nib - z never leaves int8: sum nib * x - z * sum x.  lo holds the
+      // even-k nibbles as bytes 0..15, hi16 the odd-k nibbles in the high half
+      // of each byte (16 * nib, unsigned), so their sum is 16x and one
+      // arithmetic shift restores it.
+      int se[R], so[R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) p[r] = 0;
-    if (active) {
-      const int z = j.z != nullptr ? j.z[g] : a.w_zero[j.grow * G + g];
-      const uint4 w = *reinterpret_cast<const uint4*>(wp);
-      const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-      const bool wrap = z < kWrapZero;
-      if (!wrap) {
-        // lo: the even-k nibbles as bytes 0..15; hi16: the odd-k nibbles left
-        // in the high half of each byte (16 * nib, taken as unsigned), so their
-        // dot product is 16x the true one and one arithmetic shift restores it.
+      for (int r = 0; r < R; ++r) { se[r] = 0; so[r] = 0; }
+#pragma unroll
+      for (int i = 0; i < kCpg; ++i) {
+        const int ch = 16 * ((i + rot) & (kCpg - 1));
+        const uint4 w = *reinterpret_cast<const uint4*>(wg + ch);
+        const uint32_t l0 = w.x & 0x0F0F0F0Fu, l1 = w.y & 0x0F0F0F0Fu, l2 = w.z & 0x0F0F0F0Fu, l3 = w.w & 0x0F0F0F0Fu;
+        const uint32_t h0 = w.x & 0xF0F0F0F0u, h1 = w.y & 0xF0F0F0F0u, h2 = w.z & 0xF0F0F0F0u, h3 = w.w & 0xF0F0F0F0u;
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-          const uint4 xe = *reinterpret_cast<const uint4*>(xep + r * half_k);
-          const uint4 xo = *reinterpret_cast<const uint4*>(xop + r * half_k);
-          int se = -z * sxp[r * nchunk], so = 0;
-          se = dp4a_us(wv[0] & 0x0F0F0F0Fu, xe.x, se);
-          so = dp4a_us(wv[0] & 0xF0F0F0F0u, xo.x, so);
-          se = dp4a_us(wv[1] & 0x0F0F0F0Fu, xe.y, se);
-          so = dp4a_us(wv[1] & 0xF0F0F0F0u, xo.y, so);
-          se = dp4a_us(wv[2] & 0x0F0F0F0Fu, xe.z, se);
-          so = dp4a_us(wv[2] & 0xF0F0F0F0u, xo.z, so);
-          se = dp4a_us(wv[3] & 0x0F0F0F0Fu, xe.w, se);
-          so = dp4a_us(wv[3] & 0xF0F0F0F0u, xo.w, so);
-          p[r] = se + (so >> 4);
+          const uint4 xe = *reinterpret_cast<const uint4*>(xeg + r * half_k + ch);
+          const uint4 xo = *reinterpret_cast<const uint4*>(xog + r * half_k + ch);
+          se[r] = dp4a_us(l0, xe.x, se[r]);
+          so[r] = dp4a_us(h0, xo.x, so[r]);
+          se[r] = dp4a_us(l1, xe.y, se[r]);
+          so[r] = dp4a_us(h1, xo.y, so[r]);
+          se[r] = dp4a_us(l2, xe.z, se[r]);
+          so[r] = dp4a_us(h2, xo.z, so[r]);
+          se[r] = dp4a_us(l3, xe.w, se[r]);
+          so[r] = dp4a_us(h3, xo.w, so[r]);
         }
-      } else {
-        // byte-wise (nib - z) mod 256: nib + (c & 0x7f) never carries, the top bit is an XOR
-        const uint32_t cb = static_cast<uint32_t>(-z) & 0xFFu;
-        const uint32_t c7 = (cb & 0x7Fu) * 0x01010101u;
-        const uint32_t c8 = (cb & 0x80u) * 0x01010101u;
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) p[r] = se[r] + (so[r] >> 4) - z * tt.sx[r * G + g];
+    } else {
+      // the zero point can wrap: fold every nibble to int8(nib - z) as the
+      // reference does (nib + (c & 0x7f) never carries; the top bit is an XOR)
+      const uint32_t cb = static_cast<uint32_t>(-z) & 0xFFu;
+      const uint32_t c7 = (cb & 0x7Fu) * 0x01010101u;
+      const uint32_t c8 = (cb & 0x80u) * 0x01010101u;
+#pragma unroll
+      for (int r = 0; r < R; ++r) p[r] = 0;
+#pragma unroll
+      for (int i = 0; i < kCpg; ++i) {
+        const int ch = 16 * ((i + rot) & (kCpg - 1));
+        const uint4 w = *reinterpret_cast<const uint4*>(wg + ch);
+        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
         uint32_t lo[4], hi[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          lo[q] = ((wv[q] & 0x0F0F0F0Fu) + c7) ^ c8;            // k = 8q + 0, 2, 4, 6 of the chunk
-          hi[q] = (((wv[q] >> 4) & 0x0F0F0F0Fu) + c7) ^ c8;     // k = 8q + 1, 3, 5, 7
+          lo[q] = ((wv[q] & 0x0F0F0F0Fu) + c7) ^ c8;          // k = 8q + 0, 2, 4, 6 of the chunk
+          hi[q] = (((wv[q] >> 4) & 0x0F0F0F0Fu) + c7) ^ c8;   // k = 8q + 1, 3, 5, 7
         }
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-          const uint4 xe = *reinterpret_cast<const uint4*>(xep + r * half_k);
-          const uint4 xo = *reinterpret_cast<const uint4*>(xop + r * half_k);
-          int s = 0;
+          const uint4 xe = *reinterpret_cast<const uint4*>(xeg + r * half_k + ch);
+          const uint4 xo = *reinterpret_cast<const uint4*>(xog + r * half_k + ch);
+          int s = p[r];
           s = __dp4a(static_cast<int>(lo[0]), static_cast<int>(xe.x), s);
           s = __dp4a(static_cast<int>(hi[0]), static_cast<int>(xo.x), s);
           s = __dp4a(static_cast<int>(lo[1]), static_cast<int>(xe.y), s);
@@ -172,25 +181,12 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const
         }
       }
     }
+    const float ws = j.ws != nullptr ? j.ws[g] : __ldg(a.w_scale + j.grow * G + g);
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      p[r] += __shfl_xor_sync(0xffffffffu, p[r], 1);
-      if (lpg == 4) p[r] += __shfl_xor_sync(0xffffffffu, p[r], 2);
+      acc[r] = fmaf(static_cast<float>(p[r]), ws, acc[r]);
+      if (a.partials != nullptr) a.partials[(static_cast<int64_t>(j.m0 + r) * a.N + j.n) * G + g] = p[r];
     }
-    if (active && leader) {
-      const float ws = j.ws != nullptr ? j.ws[g] : __ldg(a.w_scale + j.grow * G + g);
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        acc[r] = fmaf(static_cast<float>(p[r]), ws, acc[r]);
-        if (a.partials != nullptr) a.partials[(static_cast<int64_t>(j.m0 + r) * a.N + j.n) * G + g] = p[r];
-      }
-    }
-    wp += 512;
-    xep += 512;
-    xop += 512;
-    sxp += 32;
-    g += gstep;
-    c += 32;
   }
 #pragma unroll
   for (int r = 0; r < R; ++r) {
@@ -205,29 +201,33 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const
   }
 }
 
-// Stages the token rows [m0, m0 + rows) of x_q: per 32-value chunk, the 16
-// even-k bytes, the 16 odd-k bytes and the chunk sum.  Called by all
-// consumer threads between two consumer barriers.
+// Stages the token rows [m0, m0 + rows) of x_q: per 32-value chunk the 16
+// even-k bytes and the 16 odd-k bytes, and per K-group the sum of its
+// values.  Called by all consumer threads between two consumer barriers.
 __device__ __forceinline__ void stage_tokens(const GemmArgs& a, int m0, int rows, uint8_t* xe, uint8_t* xo, int* sx) {
   const int half_k = a.K >> 1;
-  const int nchunk = a.K >> 5;
-  for (int i = threadIdx.x; i < rows * nchunk; i += kGvConsumers * 32) {
-    const int r = i / nchunk, c = i - r * nchunk;
-    const uint4* src = reinterpret_cast<const uint4*>(a.x_q + static_cast<int64_t>(m0 + r) * a.x_stride0 + 32 * c);
-    const uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
-    const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-    uint32_t e[4], o[4];
+  const int G = a.K / a.gs;
+  const int cpg = a.gs / 32;
+  for (int i = threadIdx.x; i < rows * G; i += kGvConsumers * 32) {
+    const int r = i / G, g = i - r * G;
     int s = 0;
+    for (int cc = 0; cc < cpg; ++cc) {
+      const int c = g * cpg + cc;
+      const uint4* src = reinterpret_cast<const uint4*>(a.x_q + static_cast<int64_t>(m0 + r) * a.x_stride0 + 32 * c);
+      const uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
+      const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+      uint32_t e[4], o[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {   // 8 bytes x0..x7 -> (x0, x2, x4, x6) and (x1, x3, x5, x7)
-      e[q] = __byte_perm(wv[2 * q], wv[2 * q + 1], 0x6420);
-      o[q] = __byte_perm(wv[2 * q], wv[2 * q + 1], 0x7531);
-      s = __dp4a(static_cast<int>(wv[2 * q]), 0x01010101, s);
-      s = __dp4a(static_cast<int>(wv[2 * q + 1]), 0x01010101, s);
+      for (int q = 0; q < 4; ++q) {   // 8 bytes x0..x7 -> (x0, x2, x4, x6) and (x1, x3, x5, x7)
+        e[q] = __byte_perm(wv[2 * q], wv[2 * q + 1], 0x6420);
+        o[q] = __byte_perm(wv[2 * q], wv[2 * q + 1], 0x7531);
+        s = __dp4a(static_cast<int>(wv[2 * q]), 0x01010101, s);
+        s = __dp4a(static_cast<int>(wv[2 * q + 1]), 0x01010101, s);
+      }
+      *reinterpret_cast<uint4*>(xe + r * half_k + 16 * c) = make_uint4(e[0], e[1], e[2], e[3]);
+      *reinterpret_cast<uint4*>(xo + r * half_k + 16 * c) = make_uint4(o[0], o[1], o[2], o[3]);
     }
-    *reinterpret_cast<uint4*>(xe + r * half_k + 16 * c) = make_uint4(e[0], e[1], e[2], e[3]);
-    *reinterpret_cast<uint4*>(xo + r * half_k + 16 * c) = make_uint4(o[0], o[1], o[2], o[3]);
-    sx[r * nchunk + c] = s;
+    sx[r * G + g] = s;
   }
 }
 
@@ -291,7 +291,6 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
   } else {
     // ------------------------------------------------------------ consumers
     const TokenTile tt{s_xe, s_xo, s_sx};
-    const int lpg_shift = a.gs == 128 ? 2 : 1;
     int cur_m0 = -1, cur_rows = 0;
     int stage = 0;
     uint32_t phase = 0;
@@ -320,11 +319,20 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
         const RowJob job{st + rr * gp.row_bytes, gp.meta_bulk ? s_z + rr * G : nullptr,
                          gp.meta_bulk ? s_ws + rr * G : nullptr, tile.m0, n0 + rr,
                          static_cast<int64_t>(tile.e) * a.N + n0 + rr};
-        switch (tile.rows) {   // warp-uniform: the tile's token count
-          case 1: gv_row<1>(a, job, tt, G, lane, lpg_shift); break;
-          case 2: gv_row<2>(a, job, tt, G, lane, lpg_shift); break;
-          case 3: gv_row<3>(a, job, tt, G, lane, lpg_shift); break;
-          default: gv_row<4>(a, job, tt, G, lane, lpg_shift); break;
+        if (a.gs == 128) {
+          switch (tile.rows) {   // warp-uniform: the tile's token count
+            case 1: gv_row<1, 128>(a, job, tt, G, lane); break;
+            case 2: gv_row<2, 128>(a, job, tt, G, lane); break;
+            case 3: gv_row<3, 128>(a, job, tt, G, lane); break;
+            default: gv_row<4, 128>(a, job, tt, G, lane); break;
+          }
+        } else {
+          switch (tile.rows) {
+            case 1: gv_row<1, 64>(a, job, tt, G, lane); break;
+            case 2: gv_row<2, 64>(a, job, tt, G, lane); break;
+            case 3: gv_row<3, 64>(a, job, tt, G, lane); break;
+            default: gv_row<4, 64>(a, job, tt, G, lane); break;
+          }
         }
       }
       __syncwarp();
@@ -360,7 +368,7 @@ cudaError_t launch_gemm_gemv(const GemmArgs& a, cudaStream_t stream) {
   gp.ws_bytes = gp.meta_bulk ? gp.RB * G * 4 : 0;
   gp.z_bytes = gp.meta_bulk ? ((gp.RB * G + 15) / 16) * 16 : 0;
   gp.x_bytes = kGvRows * a.K;                    // K is a multiple of 64: both halves stay 16-byte aligned
-  gp.sx_bytes = kGvRows * (a.K / 32) * 4;
+  gp.sx_bytes = ((kGvRows * G * 4 + 15) / 16) * 16;
   const size_t stage_bytes = gp.stage_w + gp.ws_bytes + gp.z_bytes;
   const size_t fixed = 128 + gp.x_bytes + gp.sx_bytes + 2 * kGvMaxStages * 8 + 16 + sizeof(int) * 3 * (a.E + 1);
   // deepest ring that keeps two CTAs per SM, else the deepest that fits one
