@@ -94,98 +94,154 @@ struct RowJob {
   int64_t grow;          // e * N + n
 };
 
+// Exact int32 partials of NG K-groups (one lane's) whose zero points cannot
+// wrap: sum nib * x - z * sum x.  lo holds the even-k nibbles as bytes
+// 0..15, hi16 the odd-k nibbles in the high half of each byte (16 * nib,
+// unsigned), so their sum is 16x and one arithmetic shift restores it.  The
+// NG groups are independent chains the scheduler interleaves.
+template <int R, int GS, int NG>
+__device__ __forceinline__ void partials_nowrap(const uint8_t* const (&wg)[NG], const uint8_t* const (&xeg)[NG],
+                                                const uint8_t* const (&xog)[NG], int rot, int half_k,
+                                                int (&p)[NG][R], const int (&z)[NG], const int (&sxv)[NG][R]) {
+  constexpr int kCpg = GS / 32;
+  int se[NG][R], so[NG][R];
+#pragma unroll
+  for (int n = 0; n < NG; ++n)
+#pragma unroll
+    for (int r = 0; r < R; ++r) { se[n][r] = -z[n] * sxv[n][r]; so[n][r] = 0; }
+#pragma unroll
+  for (int i = 0; i < kCpg; ++i) {
+    const int ch = 16 * ((i + rot) & (kCpg - 1));
+#pragma unroll
+    for (int n = 0; n < NG; ++n) {
+      const uint4 w = *reinterpret_cast<const uint4*>(wg[n] + ch);
+      const uint32_t l0 = w.x & 0x0F0F0F0Fu, l1 = w.y & 0x0F0F0F0Fu, l2 = w.z & 0x0F0F0F0Fu, l3 = w.w & 0x0F0F0F0Fu;
+      const uint32_t h0 = w.x & 0xF0F0F0F0u, h1 = w.y & 0xF0F0F0F0u, h2 = w.z & 0xF0F0F0F0u, h3 = w.w & 0xF0F0F0F0u;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const uint4 xe = *reinterpret_cast<const uint4*>(xeg[n] + r * half_k + ch);
+        const uint4 xo = *reinterpret_cast<const uint4*>(xog[n] + r * half_k + ch);
+        se[n][r] = dp4a_us(l0, xe.x, se[n][r]);
+        so[n][r] = dp4a_us(h0, xo.x, so[n][r]);
+        se[n][r] = dp4a_us(l1, xe.y, se[n][r]);
+        so[n][r] = dp4a_us(h1, xo.y, so[n][r]);
+        se[n][r] = dp4a_us(l2, xe.z, se[n][r]);
+        so[n][r] = dp4a_us(h2, xo.z, so[n][r]);
+        se[n][r] = dp4a_us(l3, xe.w, se[n][r]);
+        so[n][r] = dp4a_us(h3, xo.w, so[n][r]);
+      }
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < NG; ++n)
+#pragma unroll
+    for (int r = 0; r < R; ++r) p[n][r] = se[n][r] + (so[n][r] >> 4);
+}
+
+// Exact int32 partial of one K-group whose zero point can wrap: every
+// nibble is folded to int8(nib - z) as the reference does (nib + (c & 0x7f)
+// never carries; the top bit is an XOR).
+template <int R, int GS>
+__device__ __forceinline__ void partials_wrap(const uint8_t* wg, const uint8_t* xeg, const uint8_t* xog, int rot,
+                                              int half_k, int z, int (&p)[R]) {
+  constexpr int kCpg = GS / 32;
+  const uint32_t cb = static_cast<uint32_t>(-z) & 0xFFu;
+  const uint32_t c7 = (cb & 0x7Fu) * 0x01010101u;
+  const uint32_t c8 = (cb & 0x80u) * 0x01010101u;
+#pragma unroll
+  for (int r = 0; r < R; ++r) p[r] = 0;
+#pragma unroll
+  for (int i = 0; i < kCpg; ++i) {
+    const int ch = 16 * ((i + rot) & (kCpg - 1));
+    const uint4 w = *reinterpret_cast<const uint4*>(wg + ch);
+    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+    uint32_t lo[4], hi[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      lo[q] = ((wv[q] & 0x0F0F0F0Fu) + c7) ^ c8;          // k = 8q + 0, 2, 4, 6 of the chunk
+      hi[q] = (((wv[q] >> 4) & 0x0F0F0F0Fu) + c7) ^ c8;   // k = 8q + 1, 3, 5, 7
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const uint4 xe = *reinterpret_cast<const uint4*>(xeg + r * half_k + ch);
+      const uint4 xo = *reinterpret_cast<const uint4*>(xog + r * half_k + ch);
+      int s = p[r];
+      s = __dp4a(static_cast<int>(lo[0]), static_cast<int>(xe.x), s);
+      s = __dp4a(static_cast<int>(hi[0]), static_cast<int>(xo.x), s);
+      s = __dp4a(static_cast<int>(lo[1]), static_cast<int>(xe.y), s);
+      s = __dp4a(static_cast<int>(hi[1]), static_cast<int>(xo.y), s);
+      s = __dp4a(static_cast<int>(lo[2]), static_cast<int>(xe.z), s);
+      s = __dp4a(static_cast<int>(hi[2]), static_cast<int>(xo.z), s);
+      s = __dp4a(static_cast<int>(lo[3]), static_cast<int>(xe.w), s);
+      s = __dp4a(static_cast<int>(hi[3]), static_cast<int>(xo.w), s);
+      p[r] = s;
+    }
+  }
+}
+
 // One weight row against R token rows (R = the tile's token count).  Lane l
-// owns K-groups l, l + 32, ...: it reads the group's GS/2 packed bytes as
+// owns K-groups l, l + 32, ...: it reads each group's GS/2 packed bytes as
 // GS/32 16-byte chunks (visited in a lane-rotated order, so the 16-byte
 // shared loads of a quarter warp hit distinct banks), forms the exact int32
-// partial on its own and applies w_scale; one warp reduction per token row
-// finishes the output.
-template <int R, int GS>
+// partials on its own and applies w_scale; one warp reduction per token row
+// finishes the output.  NG groups of a lane are in flight at once.
+template <int R, int GS, int NG>
 __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const TokenTile& tt, int G, int lane) {
-  constexpr int kCpg = GS / 32;                 // 16-byte packed chunks per group
-  constexpr int kRot = kCpg == 4 ? 1 : 2;       // lane -> chunk rotation (conflict-free quarter warps)
+  constexpr int kRot = GS == 128 ? 1 : 2;       // lane -> chunk rotation (conflict-free quarter warps)
   const int half_k = a.K >> 1;
   const int rot = lane >> kRot;
   float acc[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) acc[r] = 0.f;
-  for (int g = lane; g < G; g += 32) {
-    const int z = j.z != nullptr ? j.z[g] : a.w_zero[j.grow * G + g];
-    const uint8_t* wg = j.w + g * (GS / 2);
-    const uint8_t* xeg = tt.xe + g * (GS / 2);
-    const uint8_t* xog = tt.xo + g * (GS / 2);
-    int p[R];
-    if (z >= kWrapZero) {
-      // nib - z never leaves int8: sum nib * x - z * sum x.  lo holds the
-      // even-k nibbles as bytes 0..15, hi16 the odd-k nibbles in the high half
-      // of each byte (16 * nib, unsigned), so their sum is 16x and one
-      // arithmetic shift restores it.
-      int se[R], so[R];
+  for (int g0 = lane; g0 < G; g0 += 32 * NG) {
+    int g[NG], z[NG], sxv[NG][R];
+    bool valid[NG];
+    const uint8_t* wg[NG];
+    const uint8_t* xeg[NG];
+    const uint8_t* xog[NG];
+    bool any_wrap = false;
 #pragma unroll
-      for (int r = 0; r < R; ++r) { se[r] = 0; so[r] = 0; }
+    for (int n = 0; n < NG; ++n) {
+      valid[n] = g0 + 32 * n < G;
+      g[n] = valid[n] ? g0 + 32 * n : g0;   // an idle slot repeats the first group (result unused)
+      z[n] = j.z != nullptr ? j.z[g[n]] : a.w_zero[j.grow * G + g[n]];
+      any_wrap |= z[n] < kWrapZero;
+      wg[n] = j.w + g[n] * (GS / 2);
+      xeg[n] = tt.xe + g[n] * (GS / 2);
+      xog[n] = tt.xo + g[n] * (GS / 2);
 #pragma unroll
-      for (int i = 0; i < kCpg; ++i) {
-        const int ch = 16 * ((i + rot) & (kCpg - 1));
-        const uint4 w = *reinterpret_cast<const uint4*>(wg + ch);
-        const uint32_t l0 = w.x & 0x0F0F0F0Fu, l1 = w.y & 0x0F0F0F0Fu, l2 = w.z & 0x0F0F0F0Fu, l3 = w.w & 0x0F0F0F0Fu;
-        const uint32_t h0 = w.x & 0xF0F0F0F0u, h1 = w.y & 0xF0F0F0F0u, h2 = w.z & 0xF0F0F0F0u, h3 = w.w & 0xF0F0F0F0u;
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const uint4 xe = *reinterpret_cast<const uint4*>(xeg + r * half_k + ch);
-          const uint4 xo = *reinterpret_cast<const uint4*>(xog + r * half_k + ch);
-          se[r] = dp4a_us(l0, xe.x, se[r]);
-          so[r] = dp4a_us(h0, xo.x, so[r]);
-          se[r] = dp4a_us(l1, xe.y, se[r]);
-          so[r] = dp4a_us(h1, xo.y, so[r]);
-          se[r] = dp4a_us(l2, xe.z, se[r]);
-          so[r] = dp4a_us(h2, xo.z, so[r]);
-          se[r] = dp4a_us(l3, xe.w, se[r]);
-          so[r] = dp4a_us(h3, xo.w, so[r]);
-        }
-      }
-#pragma unroll
-      for (int r = 0; r < R; ++r) p[r] = se[r] + (so[r] >> 4) - z * tt.sx[r * G + g];
+      for (int r = 0; r < R; ++r) sxv[n][r] = tt.sx[r * G + g[n]];
+    }
+    int p[NG][R];
+    if (!any_wrap) {
+      partials_nowrap<R, GS, NG>(wg, xeg, xog, rot, half_k, p, z, sxv);
     } else {
-      // the zero point can wrap: fold every nibble to int8(nib - z) as the
-      // reference does (nib + (c & 0x7f) never carries; the top bit is an XOR)
-      const uint32_t cb = static_cast<uint32_t>(-z) & 0xFFu;
-      const uint32_t c7 = (cb & 0x7Fu) * 0x01010101u;
-      const uint32_t c8 = (cb & 0x80u) * 0x01010101u;
 #pragma unroll
-      for (int r = 0; r < R; ++r) p[r] = 0;
+      for (int n = 0; n < NG; ++n) {
+        if (z[n] < kWrapZero) {
+          partials_wrap<R, GS>(wg[n], xeg[n], xog[n], rot, half_k, z[n], p[n]);
+        } else {
+          const uint8_t* const w1[1] = {wg[n]};
+          const uint8_t* const e1[1] = {xeg[n]};
+          const uint8_t* const o1[1] = {xog[n]};
+          int p1[1][R], z1[1] = {z[n]}, s1[1][R];
 #pragma unroll
-      for (int i = 0; i < kCpg; ++i) {
-        const int ch = 16 * ((i + rot) & (kCpg - 1));
-        const uint4 w = *reinterpret_cast<const uint4*>(wg + ch);
-        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-        uint32_t lo[4], hi[4];
+          for (int r = 0; r < R; ++r) s1[0][r] = sxv[n][r];
+          partials_nowrap<R, GS, 1>(w1, e1, o1, rot, half_k, p1, z1, s1);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          lo[q] = ((wv[q] & 0x0F0F0F0Fu) + c7) ^ c8;          // k = 8q + 0, 2, 4, 6 of the chunk
-          hi[q] = (((wv[q] >> 4) & 0x0F0F0F0Fu) + c7) ^ c8;   // k = 8q + 1, 3, 5, 7
-        }
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const uint4 xe = *reinterpret_cast<const uint4*>(xeg + r * half_k + ch);
-          const uint4 xo = *reinterpret_cast<const uint4*>(xog + r * half_k + ch);
-          int s = p[r];
-          s = __dp4a(static_cast<int>(lo[0]), static_cast<int>(xe.x), s);
-          s = __dp4a(static_cast<int>(hi[0]), static_cast<int>(xo.x), s);
-          s = __dp4a(static_cast<int>(lo[1]), static_cast<int>(xe.y), s);
-          s = __dp4a(static_cast<int>(hi[1]), static_cast<int>(xo.y), s);
-          s = __dp4a(static_cast<int>(lo[2]), static_cast<int>(xe.z), s);
-          s = __dp4a(static_cast<int>(hi[2]), static_cast<int>(xo.z), s);
-          s = __dp4a(static_cast<int>(lo[3]), static_cast<int>(xe.w), s);
-          s = __dp4a(static_cast<int>(hi[3]), static_cast<int>(xo.w), s);
-          p[r] = s;
+          for (int r = 0; r < R; ++r) p[n][r] = p1[0][r];
         }
       }
     }
-    const float ws = j.ws != nullptr ? j.ws[g] : __ldg(a.w_scale + j.grow * G + g);
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      acc[r] = fmaf(static_cast<float>(p[r]), ws, acc[r]);
-      if (a.partials != nullptr) a.partials[(static_cast<int64_t>(j.m0 + r) * a.N + j.n) * G + g] = p[r];
+    for (int n = 0; n < NG; ++n) {
+      if (!valid[n]) continue;
+      const float ws = j.ws != nullptr ? j.ws[g[n]] : __ldg(a.w_scale + j.grow * G + g[n]);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        acc[r] = fmaf(static_cast<float>(p[n][r]), ws, acc[r]);
+        if (a.partials != nullptr) a.partials[(static_cast<int64_t>(j.m0 + r) * a.N + j.n) * G + g[n]] = p[n][r];
+      }
     }
   }
 #pragma unroll
@@ -321,17 +377,17 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
                          static_cast<int64_t>(tile.e) * a.N + n0 + rr};
         if (a.gs == 128) {
           switch (tile.rows) {   // warp-uniform: the tile's token count
-            case 1: gv_row<1, 128>(a, job, tt, G, lane); break;
-            case 2: gv_row<2, 128>(a, job, tt, G, lane); break;
-            case 3: gv_row<3, 128>(a, job, tt, G, lane); break;
-            default: gv_row<4, 128>(a, job, tt, G, lane); break;
+            case 1: gv_row<1, 128, 2>(a, job, tt, G, lane); break;
+            case 2: gv_row<2, 128, 2>(a, job, tt, G, lane); break;
+            case 3: gv_row<3, 128, 1>(a, job, tt, G, lane); break;
+            default: gv_row<4, 128, 1>(a, job, tt, G, lane); break;
           }
         } else {
           switch (tile.rows) {
-            case 1: gv_row<1, 64>(a, job, tt, G, lane); break;
-            case 2: gv_row<2, 64>(a, job, tt, G, lane); break;
-            case 3: gv_row<3, 64>(a, job, tt, G, lane); break;
-            default: gv_row<4, 64>(a, job, tt, G, lane); break;
+            case 1: gv_row<1, 64, 2>(a, job, tt, G, lane); break;
+            case 2: gv_row<2, 64, 2>(a, job, tt, G, lane); break;
+            case 3: gv_row<3, 64, 1>(a, job, tt, G, lane); break;
+            default: gv_row<4, 64, 1>(a, job, tt, G, lane); break;
           }
         }
       }
