@@ -330,4 +330,33 @@ __device__ __forceinline__ Tile sched_tile(const TileSched& s, int t) {
   return r;
 }
 
+// Walks consecutive tiles t, t+1, ... without a search per tile: tiles are
+// numbered expert by expert, weight block (slow) by token block (fast).
+struct TileWalk {
+  const TileSched* s;
+  Tile cur;
+  int tb, tbs;
+  __device__ __forceinline__ void start(const TileSched& sch, int t) {
+    s = &sch;
+    cur = sched_tile(sch, t);
+    tbs = (sch.cnt[cur.e] + sch.bt - 1) / sch.bt;
+    tb = (cur.m0 - sch.seg[cur.e]) / sch.bt;
+  }
+  // Advance to the next tile (the caller keeps it below the tile total).
+  __device__ __forceinline__ void next() {
+    if (++tb < tbs) {
+      cur.m0 += s->bt;
+    } else if (tb = 0, ++cur.nb < s->NB) {
+      cur.m0 = s->seg[cur.e];
+    } else {
+      cur.nb = 0;
+      do { ++cur.e; } while (cur.e < s->E - 1 && s->prefix[cur.e + 1] == s->prefix[cur.e]);
+      tbs = (s->cnt[cur.e] + s->bt - 1) / s->bt;
+      cur.m0 = s->seg[cur.e];
+    }
+    const int left = s->cnt[cur.e] - tb * s->bt;
+    cur.rows = left < s->bt ? left : s->bt;
+  }
+};
+
 }  // namespace w4a8

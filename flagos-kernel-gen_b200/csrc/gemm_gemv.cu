@@ -325,8 +325,11 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
       const uint64_t pol = policy_evict_first();
       int stage = 0;
       uint32_t phase = 0;
+      TileWalk walk;
+      if (t_begin < t_end) walk.start(sch, t_begin);
       for (int t = t_begin; t < t_end; ++t) {
-        const Tile tile = sched_tile(sch, t);
+        if (t > t_begin) walk.next();
+        const Tile tile = walk.cur;
         const int n0 = tile.nb * gp.RB;
         const int rows = min(gp.RB, a.N - n0);
         const int64_t row0 = static_cast<int64_t>(tile.e) * a.N + n0;
@@ -352,8 +355,11 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
     uint32_t phase = 0;
     bool failed = false;   // after a timed-out wait, keep walking the tiles (no work) so the
                            // consumer barriers below still see every consumer warp
+    TileWalk walk;
+    if (t_begin < t_end) walk.start(sch, t_begin);
     for (int t = t_begin; t < t_end; ++t) {
-      const Tile tile = sched_tile(sch, t);
+      if (t > t_begin) walk.next();
+      const Tile tile = walk.cur;
       if (tile.m0 != cur_m0 || tile.rows != cur_rows) {   // uniform over the consumers
         consumers_sync();                                 // nobody still reads the old rows
         stage_tokens(a, tile.m0, tile.rows, s_xe, s_xo, s_sx);
