@@ -159,23 +159,25 @@ int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_
       e = launch_gemm_simt(a, st);
       break;
     default: {  // W4A8_KERNEL_AUTO
-      // Experts with at most kGemvMaxTokens rows are weight-streaming bound and
-      // go to the streaming kernel, the others to the tensor-core kernel.  The
-      // split is applied on the device by each kernel's scheduler (row-count
-      // window), so no host synchronisation is needed; a launch whose window
-      // holds no expert exits after its prologue.
+      // Experts with at most kGemvAutoRows rows are weight-streaming bound and
+      // go to the streaming kernel, the others to the tensor-core kernel
+      // (measured on B200: at 5-8 rows per expert a second streaming pass costs
+      // more than the tensor-core tiles).  The split is applied on
+      // the device by each kernel's scheduler (row-count window), so no host
+      // synchronisation is needed; a launch whose window holds no expert exits
+      // after its prologue.
       if (!tc_ok) {
-        if (gemv_ok && M_total <= kGemvMaxTokens) e = launch_gemm_gemv(a, st);
+        if (gemv_ok && M_total <= kGemvAutoRows) e = launch_gemm_gemv(a, st);
         else if (simt_ok) e = launch_gemm_simt(a, st);
         else return fail(W4A8_ERR_INVALID, "x_q rows must be at least 4-byte aligned");
-      } else if (M_total <= kGemvMaxTokens) {
+      } else if (M_total <= kGemvAutoRows) {
         e = launch_gemm_gemv(a, st);
       } else if (M_total >= 64 * E) {
         e = launch_gemm_tc(a, st);
       } else {
         GemmArgs small = a, big = a;
-        small.max_rows = kGemvMaxTokens;
-        big.min_rows = kGemvMaxTokens + 1;
+        small.max_rows = kGemvAutoRows;
+        big.min_rows = kGemvAutoRows + 1;
         e = launch_gemm_gemv(small, st);
         if (e == cudaSuccess) e = launch_gemm_tc(big, st);
       }

@@ -244,7 +244,8 @@ __host__ __device__ constexpr uint32_t make_idesc_i8(int m, int n) {
 // tb of up to `bt` rows of that expert's segment).  Tiles are numbered expert
 // by expert; inside an expert nb is the slow index and tb the fast one, so
 // tiles that share a weight block run on neighbouring CTAs at the same time
-// and the second read of the weight block hits L2.
+// and the second read of the weight block hits L2 (tb_slow flips the order,
+// for a kernel that keeps the token block resident instead).
 //
 // Segment semantics follow the reference loop (docs/Task1.md:88-96): rows
 // [off[e], off[e+1]) belong to expert e; empty or inverted segments are
@@ -257,6 +258,7 @@ struct TileSched {
   int E, bt, NB;
   int min_rows = 1;           // experts with fewer rows are left to another kernel
   int max_rows = 0x7fffffff;  // experts with more rows are left to another kernel
+  bool tb_slow = false;       // token block as the slow index inside an expert
 };
 
 // Must be called by all threads of the CTA (contains __syncthreads()).
@@ -322,8 +324,14 @@ __device__ __forceinline__ Tile sched_tile(const TileSched& s, int t) {
   const int tbs = (s.cnt[e] + s.bt - 1) / s.bt;
   Tile r;
   r.e = e;
-  r.nb = local / tbs;
-  const int tb = local - r.nb * tbs;
+  int tb;
+  if (s.tb_slow) {
+    tb = local / s.NB;
+    r.nb = local - tb * s.NB;
+  } else {
+    r.nb = local / tbs;
+    tb = local - r.nb * tbs;
+  }
   r.m0 = s.seg[e] + tb * s.bt;
   const int left = s.cnt[e] - tb * s.bt;
   r.rows = left < s.bt ? left : s.bt;
@@ -344,7 +352,18 @@ struct TileWalk {
   }
   // Advance to the next tile (the caller keeps it below the tile total).
   __device__ __forceinline__ void next() {
-    if (++tb < tbs) {
+    if (s->tb_slow) {
+      if (++cur.nb < s->NB) {
+        // same token block
+      } else if (cur.nb = 0, ++tb < tbs) {
+        cur.m0 += s->bt;
+      } else {
+        tb = 0;
+        do { ++cur.e; } while (cur.e < s->E - 1 && s->prefix[cur.e + 1] == s->prefix[cur.e]);
+        tbs = (s->cnt[cur.e] + s->bt - 1) / s->bt;
+        cur.m0 = s->seg[cur.e];
+      }
+    } else if (++tb < tbs) {
       cur.m0 += s->bt;
     } else if (tb = 0, ++cur.nb < s->NB) {
       cur.m0 = s->seg[cur.e];

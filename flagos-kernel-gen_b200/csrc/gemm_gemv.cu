@@ -309,8 +309,9 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
     *abort_flag = 0;
     fence_mbar_init();
   }
+  // token block as the slow index: a CTA stages each block's token rows once
   TileSched sch{sched_mem, sched_mem + (a.E + 1), sched_mem + 2 * (a.E + 1), a.E, kGvRows,
-                (a.N + gp.RB - 1) / gp.RB, a.min_rows, a.max_rows};
+                (a.N + gp.RB - 1) / gp.RB, a.min_rows, a.max_rows, true};
   const int total = sched_build(sch, a.offsets, a.M_total);   // contains __syncthreads
   const int G = a.K / a.gs;
   // Each CTA takes a contiguous range of blocks: consecutive blocks belong to

@@ -31,6 +31,7 @@ struct GemmArgs {
 cudaError_t launch_gemm_simt(const GemmArgs& a, cudaStream_t stream);
 cudaError_t launch_gemm_gemv(const GemmArgs& a, cudaStream_t stream);
 constexpr int kGemvMaxTokens = 4;  // tokens per pass of the streaming kernel
+constexpr int kGemvAutoRows = 4;   // AUTO dispatch: experts with at most this many rows stream
 cudaError_t launch_gemm_tc(const GemmArgs& a, cudaStream_t stream);
 bool gemm_tc_supports(int K, int gs, int E);
 

@@ -45,6 +45,7 @@ class CudaEPOps:
         return cuda_ops.gather_rows(src, index)
 
     def grouped_gemm(self, xq, xs, w: W4A8Weights, offsets, out, gs):
+        self.gemm_launches += len(cuda_ops.gemm_auto_kernels(xq.shape[0], w.packed.shape[0]))
         return cuda_ops.w4a8_group_gemm_moe(xq, xs, w.packed, w.scale, w.zero, offsets, out, gs)
 
     def silu_mul_requant(self, h):
@@ -53,9 +54,12 @@ class CudaEPOps:
     def combine(self, y, inv_pos, topk_w):
         return cuda_ops.moe_combine(y, inv_pos, topk_w)
 
-    # launches of this package's kernels per forward: align x2 (3 each), quant_scatter,
-    # 3 row gathers (rows, scales, outputs), 2 GEMMs, SiLU-mul requant, combine
-    launches_per_forward = 6 + 1 + 3 + 2 + 1 + 1
+    # launches of this package's kernels per forward besides the grouped GEMMs:
+    # align x2 (3 each), quant_scatter, 3 row gathers (rows, scales, outputs),
+    # SiLU-mul requant, combine; the GEMMs (1 or 2 launches each, AUTO dispatch)
+    # are counted as they are issued
+    fixed_launches_per_forward = 6 + 1 + 3 + 1 + 1
+    gemm_launches = 0
 
 
 class ExpertParallelMoE:
@@ -74,13 +78,15 @@ class ExpertParallelMoE:
             raise ValueError("w13_local must hold this rank's E/P experts")
         self.w13, self.w2 = w13_local, w2_local
         self.gs, self.topk = group_size, topk
+        self._last_gemm_launches = 0
         self.ops = ops if ops is not None else CudaEPOps()
         self.offsets = None          # last local expert offsets (for reporting)
         self.out = w13_local.packed.new_empty((0,))
 
     # -- helpers ---------------------------------------------------------------
     def launches_per_forward(self) -> int:
-        return getattr(self.ops, "launches_per_forward", 0)
+        """Library launches of the last forward (0 for a backend that is not the CUDA library)."""
+        return getattr(self.ops, "fixed_launches_per_forward", 0) + self._last_gemm_launches
 
     @property
     def local(self):
@@ -97,6 +103,7 @@ class ExpertParallelMoE:
         k = self.topk
         dev = x.device
         ops = self.ops
+        g0 = getattr(ops, "gemm_launches", 0)
         ids = topk_ids.to(torch.int32)
         # 1. destination rank of every slot; ids outside [0, E) are dropped (-1)
         dest = torch.where((ids >= 0) & (ids < self.E), ids // self.epr, torch.full_like(ids, -1))
@@ -149,6 +156,7 @@ class ExpertParallelMoE:
             y_full = torch.empty((T * k, y_home.shape[1]), dtype=torch.bfloat16, device=dev)
             y_full[:n_send] = y_home
         self.out = ops.combine(y_full, send_inv, topk_weights)
+        self._last_gemm_launches = getattr(ops, "gemm_launches", 0) - g0
         return self.out
 
     __call__ = forward

@@ -106,9 +106,12 @@ class MoELayer:
         self.out = torch.empty((max_tokens, H if self.ffn else I), dtype=torch.bfloat16, device=dev)
 
     # number of library kernel launches per forward (for launch accounting)
-    def launches_per_forward(self) -> int:
-        # align: 3, quant_scatter: 1, gemm: 1 (+1), silu: (1), combine: 1
-        return 3 + 1 + 1 + (2 if self.ffn else 0) + 1
+    def launches_per_forward(self, tokens: int | None = None) -> int:
+        # align: 3, quant_scatter: 1, each grouped GEMM: 1 or 2 (AUTO dispatch),
+        # silu: (1), combine: 1
+        R = (tokens if tokens is not None else self.max_tokens) * self.topk
+        g = len(ops.gemm_auto_kernels(R, self.E))
+        return 3 + 1 + g + ((1 + g) if self.ffn else 0) + 1
 
     def forward(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
                 out: torch.Tensor | None = None, events: list | None = None) -> torch.Tensor:

@@ -77,6 +77,21 @@ def _gemm_operands(x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, o
     return dev, x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, M_total, E, N, K
 
 
+GEMV_AUTO_ROWS = 4   # AUTO: experts with at most this many rows take the streaming kernel
+
+
+def gemm_auto_kernels(m_total: int, num_experts: int) -> tuple[str, ...]:
+    """Kernels the AUTO dispatch of the library launches for a grouped GEMM of
+    ``m_total`` rows over ``num_experts`` experts (the host-side rule of
+    ``w4a8_group_gemm_moe_ex``; the per-expert split is then made on the
+    device).  Used for launch accounting and roofline labels."""
+    if m_total <= GEMV_AUTO_ROWS:
+        return ("gemm_gemv_kernel",)
+    if m_total >= 64 * num_experts:
+        return ("gemm_tc_kernel",)
+    return ("gemm_gemv_kernel", "gemm_tc_kernel")
+
+
 def w4a8_group_gemm_moe(
     x_q: torch.Tensor,
     x_scale: torch.Tensor,
