@@ -67,9 +67,10 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t tx
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(tx)
                : "memory");
 }
-// try_wait without an explicit suspend-time hint.  (Measured on B200: with a
-// 10 ms suspendTimeHint the tensor-core kernel produced wrong partials for a
-// fraction of its tiles, and it was no faster; the system default is used.)
+// try_wait with the system's default suspend limit (a 10 ms suspendTimeHint
+// measured no faster on B200).  Every waiter in this library uses it, the MMA
+// issuer included: a waiting try_wait hands off in ~125 cycles on B200 against
+// ~170 for a test_wait polling loop.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -90,35 +91,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (*abort_flag) return false;
-    if (clock64() - t0 > W4A8_WAIT_LIMIT_CYCLES) {
-      atomicCAS(status, 0, code);
-      *abort_flag = 1;
-      return false;
-    }
-  }
-  return true;
-}
-
-// Non-suspending probe and a bounded spin on it.  Used by the single thread
-// that issues MMAs: a suspended waiter takes ~250 cycles to wake after the
-// phase completes, which would sit directly on the tensor-core critical path.
-__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, int* status, int code,
-                                          volatile int* abort_flag) {
-  if (mbar_test_wait(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_test_wait(bar, parity)) {
     if (*abort_flag) return false;
     if (clock64() - t0 > W4A8_WAIT_LIMIT_CYCLES) {
       atomicCAS(status, 0, code);
