@@ -13,14 +13,15 @@
 // the M side every epilogue thread owns one output channel, so the per-group
 // weight scale is one register per thread.
 //
-// Per K-group accumulators: the first MMA of a group overwrites its TMEM
-// accumulator (enable-input-d off), the rest accumulate, so TMEM holds the
-// exact int32 partial P.  Exact int32 -> fp32 without I2F: the epilogue adds
-// the bit pattern of 1.5 * 2^23 (0x4B400000) to P; for |P| < 2^22 (|P| <= 2^21
-// here) the sum read as fp32 is exactly 1.5 * 2^23 + P, and one exact FSUB
-// recovers float(P).  Scale accumulation then uses packed fp32x2 FSUB/FFMA,
-// which round exactly like the scalar fmaf of the CUDA-core kernel (both
-// kernels produce identical bits).
+// Per K-group accumulators, seeded by the tensor core: each group starts with
+// one bf16 MMA (enable-input-d off) whose operands are constant atoms in
+// shared memory and whose fp32 result is 1.5 * 2^23 in every element; the
+// int8 MMAs then add the integer partial P to those bits.  For |P| < 2^22
+// (|P| <= 2^21 here) the sum read as fp32 is exactly 1.5 * 2^23 + P, so one
+// exact FSUB recovers float(P) - no quarter-rate I2F, no TMEM stores and no
+// integer add in the epilogue.  Scale accumulation then uses packed fp32x2
+// FSUB/FFMA, which round exactly like the scalar fmaf of the CUDA-core kernel
+// (both kernels produce identical bits).
 //
 // Warp roles (512 threads, one CTA per SM, persistent over tiles):
 //   warp 0      TMA producer of token tiles [rows x 128 B] (128-byte swizzle)
@@ -72,7 +73,8 @@ constexpr int kEpiCols = kBT / 2;           // columns per epilogue warpgroup
 constexpr uint32_t kMagicBits = 0x4B400000u;  // 1.5 * 2^23
 constexpr float kMagic = 12582912.0f;
 
-constexpr size_t kSmemTiles = size_t(kXStages) * kXBytes + size_t(kAStages) * kABytes +
+constexpr int kSeedBytes = 2048;   // two 1 KB swizzle atoms holding the accumulator-seed operands
+constexpr size_t kSmemTiles = size_t(kSeedBytes) + size_t(kXStages) * kXBytes + size_t(kAStages) * kABytes +
                               size_t(kWStages) * kWBytes;
 constexpr int kNumBars = 2 * kXStages + 2 * kWStages + 2 * kAStages + 4;
 
@@ -104,6 +106,21 @@ __device__ __forceinline__ void tmem_ld_x32_wait(uint32_t taddr, uint32_t (&r)[3
       : "memory");
 }
 
+// D[tmem] = A * B^T with bf16 operands and an fp32 result (enable-input-d off).
+__device__ __forceinline__ void mma_bf16_ss_overwrite(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, 0, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc)
+      : "memory");
+}
+// Instruction descriptor for kind::f16: bf16 x bf16 -> f32, both operands K-major.
+__host__ __device__ constexpr uint32_t make_idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
 __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
@@ -130,7 +147,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   uint8_t* sX = base;
   uint8_t* sA = sX + kXStages * kXBytes;
   uint8_t* sW = sA + kAStages * kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + kWStages * kWBytes);
+  uint8_t* sSeed = sW + kWStages * kWBytes;   // [A atom | B atom], 1024-aligned
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sSeed + kSeedBytes);
   uint64_t* x_full = bars;
   uint64_t* x_empty = x_full + kXStages;
   uint64_t* w_full = x_empty + kXStages;
@@ -176,6 +194,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     tc_fence_before();
   }
 
+  // Seed operands: every 16-byte chunk of the A atom holds bf16 (1, 0 x 7) and
+  // of the B atom bf16 (0.75 * 2^23, 0 x 7); a K = 16 product of them is
+  // 2 * 0.75 * 2^23 = 1.5 * 2^23, written to every accumulator element by one
+  // MMA whose row-group stride is 0 (all row groups read the same atom).
+  for (int i = threadIdx.x; i < kSeedBytes / 16; i += kThreads)
+    reinterpret_cast<uint4*>(sSeed)[i] = make_uint4(i < 64 ? 0x3F80u : 0x4AC0u, 0u, 0u, 0u);
+  fence_proxy_async_smem();
   TileSched sch{sched_mem, sched_mem + (a.E + 1), sched_mem + 2 * (a.E + 1), a.E, kBT,
                 (a.N + kBW - 1) / kBW, a.min_rows, a.max_rows};
   const int total = sched_build(sch, a.offsets, a.M_total);  // contains __syncthreads
@@ -243,12 +268,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     if (lane == 0) {
       const uint64_t desc_x0 = make_desc_sw128(smem_u32(sX));
       const uint64_t desc_a0 = make_desc_sw128(smem_u32(sA));
+      constexpr uint64_t kSboMask = ~(static_cast<uint64_t>(0x3FFF) << 32);
+      const uint64_t seed_a = make_desc_sw128(smem_u32(sSeed)) & kSboMask;          // row-group stride 0
+      const uint64_t seed_b = make_desc_sw128(smem_u32(sSeed + 1024)) & kSboMask;
       int stage = 0, astage = 0, buf = 0;
       uint32_t phase = 0, aphase = 0, bphase = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         const Tile tile = sched_tile(sch, t);
         const int n_mma = (tile.rows + 15) & ~15;
         const uint32_t idesc = make_idesc_i8(kBW, n_mma);
+        const uint32_t idesc_seed = make_idesc_bf16(kBW, n_mma);
         int sub = 0;   // group within the K block (gs = 64: two groups per block)
         for (int g = 0; g < G; ++g) {
           if (sub == 0) {
@@ -262,8 +291,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
           // descriptors advance by (byte offset >> 4) in their start-address field
           const uint64_t adesc = desc_a0 + static_cast<uint64_t>((astage * kABytes + sub * kpg * 32) >> 4);
           const uint64_t bdesc = desc_x0 + static_cast<uint64_t>((stage * kXBytes + sub * kpg * 32) >> 4);
-          for (int ks = 0; ks < kpg; ++ks)   // the group's first K step overwrites the accumulator
-            mma_i8_ss(d_tmem, adesc + 2 * ks, bdesc + 2 * ks, idesc, ks > 0 ? 1u : 0u);
+          // seed: every accumulator element = bits of 1.5 * 2^23; the int8 MMAs then add P
+          mma_bf16_ss_overwrite(d_tmem, seed_a, seed_b, idesc_seed);
+          for (int ks = 0; ks < kpg; ++ks)
+            mma_i8_ss(d_tmem, adesc + 2 * ks, bdesc + 2 * ks, idesc, 1u);
           mma_commit(&tmem_full[buf]);
           buf ^= 1;
           if (buf == 0) bphase ^= 1;
@@ -392,7 +423,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
           if (have) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {   // P + 1.5 * 2^23 read as fp32, minus 1.5 * 2^23 = float(P)
-              const uint64_t p2 = f2_sub(u2_pack(v[2 * j] + kMagicBits, v[2 * j + 1] + kMagicBits), magic2);
+              const uint64_t p2 = f2_sub(u2_pack(v[2 * j], v[2 * j + 1]), magic2);
               acc[c32 * 16 + j] = f2_fma(p2, ws2, acc[c32 * 16 + j]);
             }
             if (a.partials != nullptr && valid) {
@@ -400,7 +431,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
               for (int j = 0; j < 32; ++j) {
                 const int col = wg * kEpiCols + c32 * 32 + j;
                 if (col < tile.rows)
-                  a.partials[(static_cast<int64_t>(tile.m0 + col) * a.N + n) * G + g] = static_cast<int>(v[j]);
+                  a.partials[(static_cast<int64_t>(tile.m0 + col) * a.N + n) * G + g] = static_cast<int>(v[j] - kMagicBits);
               }
             }
           }
