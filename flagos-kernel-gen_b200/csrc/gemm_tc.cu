@@ -25,7 +25,8 @@
 //
 // Warp roles (512 threads, one CTA per SM, persistent over tiles):
 //   warp 0      TMA producer of token tiles [rows x 128 B] (128-byte swizzle)
-//   warp 1      TMEM allocator + single-thread MMA issuer
+//   warps 1, 3  MMA issuers, one thread each, one per TMEM accumulator (warp 1
+//               also allocates TMEM)
 //   warp 2      TMA producer of packed weight tiles [128 rows x 64 B] (64-byte
 //               swizzle), running ahead on its own deeper ring
 //   warps 4-7   transform: thread r unpacks weight row r (nibble order of
@@ -88,20 +89,24 @@ __device__ __forceinline__ uint32_t pack_fold(uint32_t nib4, uint32_t c7, uint32
   return (nib4 + c7) ^ c8;
 }
 
-// 32 lanes x 32 columns, followed by the wait in the same asm statement: the
-// destination registers are only written when the asynchronous load lands, so
-// the compiler must not see them as defined before the wait.
-__device__ __forceinline__ void tmem_ld_x32_wait(uint32_t taddr, uint32_t (&r)[32]) {
+// 32 lanes x 32 columns as 16 packed column pairs for the fp32x2 math.  The
+// wait sits in the same asm statement as the load (the registers are only
+// written when the load lands, so nothing may read them before the wait),
+// and so do the pairing moves, which lets the register allocator place the
+// loaded columns as aligned pairs.
+__device__ __forceinline__ void tmem_ld_x32_pairs(uint32_t taddr, uint64_t (&d)[16]) {
   asm volatile(
+      "{\n\t.reg .b32 t<32>;\n\t"
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      "{t0,t1,t2,t3,t4,t5,t6,t7,t8,t9,t10,t11,t12,t13,t14,t15,"
+      "t16,t17,t18,t19,t20,t21,t22,t23,t24,t25,t26,t27,t28,t29,t30,t31}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n\t"
+      "mov.b64 %0, {t0, t1};\n\tmov.b64 %1, {t2, t3};\n\tmov.b64 %2, {t4, t5};\n\tmov.b64 %3, {t6, t7};\n\t"
+      "mov.b64 %4, {t8, t9};\n\tmov.b64 %5, {t10, t11};\n\tmov.b64 %6, {t12, t13};\n\tmov.b64 %7, {t14, t15};\n\t"
+      "mov.b64 %8, {t16, t17};\n\tmov.b64 %9, {t18, t19};\n\tmov.b64 %10, {t20, t21};\n\tmov.b64 %11, {t22, t23};\n\t"
+      "mov.b64 %12, {t24, t25};\n\tmov.b64 %13, {t26, t27};\n\tmov.b64 %14, {t28, t29};\n\tmov.b64 %15, {t30, t31};\n\t}"
+      : "=l"(d[0]), "=l"(d[1]), "=l"(d[2]), "=l"(d[3]), "=l"(d[4]), "=l"(d[5]), "=l"(d[6]), "=l"(d[7]),
+        "=l"(d[8]), "=l"(d[9]), "=l"(d[10]), "=l"(d[11]), "=l"(d[12]), "=l"(d[13]), "=l"(d[14]), "=l"(d[15])
       : "r"(taddr)
       : "memory");
 }
@@ -134,9 +139,6 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
   return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
 }
-__device__ __forceinline__ uint64_t u2_pack(uint32_t lo, uint32_t hi) {
-  return static_cast<uint64_t>(lo) | (static_cast<uint64_t>(hi) << 32);
-}
 
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
@@ -165,9 +167,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   const int lane = lane_id();
 
   if (threadIdx.x == 0) {
+    const int groups_per_block = kBK / a.gs;   // MMA issuers (one per group) that read a K block
     for (int s = 0; s < kXStages; ++s) {
       mbar_init(&x_full[s], 1);
-      mbar_init(&x_empty[s], 1);   // MMA commit
+      mbar_init(&x_empty[s], groups_per_block);   // one MMA commit per group of the block
     }
     for (int s = 0; s < kWStages; ++s) {
       mbar_init(&w_full[s], 1);
@@ -175,7 +178,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     }
     for (int s = 0; s < kAStages; ++s) {
       mbar_init(&a_full[s], 4);
-      mbar_init(&a_empty[s], 1);
+      mbar_init(&a_empty[s], groups_per_block);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tmem_full[b], 1);
@@ -263,15 +266,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
       }
     w_done:;
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == 3) {
+    // ------------------------------------------------------------ MMA issuers
+    // Two issuing threads, one per TMEM accumulator: thread p issues the
+    // groups c with c % 2 == p (c counts this CTA's groups), so one thread's
+    // waits and commits overlap the other's MMAs.  Each group's MMAs read one
+    // K block; its issuer commits the block's release once per group (a block
+    // of two gs = 64 groups is released by both issuers; a trailing block
+    // with one group is committed twice by its issuer).
     if (lane == 0) {
+      const int p = warp == 1 ? 0 : 1;
       const uint64_t desc_x0 = make_desc_sw128(smem_u32(sX));
       const uint64_t desc_a0 = make_desc_sw128(smem_u32(sA));
       constexpr uint64_t kSboMask = ~(static_cast<uint64_t>(0x3FFF) << 32);
       const uint64_t seed_a = make_desc_sw128(smem_u32(sSeed)) & kSboMask;          // row-group stride 0
       const uint64_t seed_b = make_desc_sw128(smem_u32(sSeed + 1024)) & kSboMask;
-      int stage = 0, astage = 0, buf = 0;
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(p * kBT);
+      int stage = 0, astage = 0, c = 0;
       uint32_t phase = 0, aphase = 0, bphase = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         const Tile tile = sched_tile(sch, t);
@@ -279,31 +290,36 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         const uint32_t idesc = make_idesc_i8(kBW, n_mma);
         const uint32_t idesc_seed = make_idesc_bf16(kBW, n_mma);
         int sub = 0;   // group within the K block (gs = 64: two groups per block)
-        for (int g = 0; g < G; ++g) {
-          if (sub == 0) {
+        for (int g = 0; g < G; ++g, ++c) {
+          const bool block_end = (sub + 1 == gpk) || g == G - 1;
+          if ((c & 1) == p) {
             if (!mbar_wait(&x_full[stage], phase, a.status, kDevTimeoutLoadFull, abort_flag)) goto mma_done;
             if (!mbar_wait(&a_full[astage], aphase, a.status, kDevTimeoutAFull, abort_flag)) goto mma_done;
-          }
-          if (!mbar_wait(&tmem_empty[buf], bphase ^ 1, a.status, kDevTimeoutTmemEmpty, abort_flag))
-            goto mma_done;
-          tc_fence_after();
-          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kBT);
-          // descriptors advance by (byte offset >> 4) in their start-address field
-          const uint64_t adesc = desc_a0 + static_cast<uint64_t>((astage * kABytes + sub * kpg * 32) >> 4);
-          const uint64_t bdesc = desc_x0 + static_cast<uint64_t>((stage * kXBytes + sub * kpg * 32) >> 4);
-          // seed: every accumulator element = bits of 1.5 * 2^23; the int8 MMAs then add P
-          mma_bf16_ss_overwrite(d_tmem, seed_a, seed_b, idesc_seed);
-          for (int ks = 0; ks < kpg; ++ks)
-            mma_i8_ss(d_tmem, adesc + 2 * ks, bdesc + 2 * ks, idesc, 1u);
-          mma_commit(&tmem_full[buf]);
-          buf ^= 1;
-          if (buf == 0) bphase ^= 1;
-          if (++sub == gpk || g == G - 1) {
-            sub = 0;
+            if (!mbar_wait(&tmem_empty[p], bphase ^ 1, a.status, kDevTimeoutTmemEmpty, abort_flag))
+              goto mma_done;
+            tc_fence_after();
+            // descriptors advance by (byte offset >> 4) in their start-address field
+            const uint64_t adesc = desc_a0 + static_cast<uint64_t>((astage * kABytes + sub * kpg * 32) >> 4);
+            const uint64_t bdesc = desc_x0 + static_cast<uint64_t>((stage * kXBytes + sub * kpg * 32) >> 4);
+            // seed: every accumulator element = bits of 1.5 * 2^23; the int8 MMAs then add P
+            mma_bf16_ss_overwrite(d_tmem, seed_a, seed_b, idesc_seed);
+            for (int ks = 0; ks < kpg; ++ks)
+              mma_i8_ss(d_tmem, adesc + 2 * ks, bdesc + 2 * ks, idesc, 1u);
+            mma_commit(&tmem_full[p]);
+            bphase ^= 1;
             mma_commit(&x_empty[stage]);
             mma_commit(&a_empty[astage]);
+            if (block_end && sub + 1 < gpk) {   // a trailing block with fewer groups than its count
+              mma_commit(&x_empty[stage]);
+              mma_commit(&a_empty[astage]);
+            }
+          }
+          if (block_end) {
+            sub = 0;
             if (++stage == kXStages) { stage = 0; phase ^= 1; }
             if (++astage == kAStages) { astage = 0; aphase ^= 1; }
+          } else {
+            ++sub;
           }
         }
       }
@@ -412,9 +428,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
 #pragma unroll
         for (int c32 = 0; c32 < kEpiCols / 32; ++c32) {
           const bool have = c32 * 32 < my_cols;   // warp-uniform
-          uint32_t v[32];
+          uint64_t d[16];
           __syncwarp();
-          if (have) tmem_ld_x32_wait(taddr + c32 * 32, v);
+          if (have) tmem_ld_x32_pairs(taddr + c32 * 32, d);
           if (c32 == kEpiCols / 32 - 1) {
             tc_fence_before();
             __syncwarp();
@@ -422,16 +438,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
           }
           if (have) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {   // P + 1.5 * 2^23 read as fp32, minus 1.5 * 2^23 = float(P)
-              const uint64_t p2 = f2_sub(u2_pack(v[2 * j], v[2 * j + 1]), magic2);
-              acc[c32 * 16 + j] = f2_fma(p2, ws2, acc[c32 * 16 + j]);
-            }
+            for (int j = 0; j < 16; ++j)   // P + 1.5 * 2^23 read as fp32, minus 1.5 * 2^23 = float(P)
+              acc[c32 * 16 + j] = f2_fma(f2_sub(d[j], magic2), ws2, acc[c32 * 16 + j]);
             if (a.partials != nullptr && valid) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
                 const int col = wg * kEpiCols + c32 * 32 + j;
+                const uint32_t vj = static_cast<uint32_t>(d[j >> 1] >> (32 * (j & 1)));
                 if (col < tile.rows)
-                  a.partials[(static_cast<int64_t>(tile.m0 + col) * a.N + n) * G + g] = static_cast<int>(v[j] - kMagicBits);
+                  a.partials[(static_cast<int64_t>(tile.m0 + col) * a.N + n) * G + g] = static_cast<int>(vj - kMagicBits);
               }
             }
           }
