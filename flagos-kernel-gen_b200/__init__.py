@@ -22,12 +22,13 @@ from .ops import (  # noqa: F401
     w4a8_group_gemm_moe,
     w4a8_group_gemm_moe_ex,
 )
-from .moe import MoELayer, W4A8Weights, w4a8_moe  # noqa: F401
+from .moe import HostPipeline, MoELayer, W4A8Weights, w4a8_moe  # noqa: F401
 from ._lib import KERNEL_AUTO, KERNEL_GEMV, KERNEL_SIMT, KERNEL_TC  # noqa: F401
 from . import ops, workloads  # noqa: F401
 
 __all__ = [
     "w4a8_group_gemm_moe", "w4a8_group_gemm_moe_ex", "act_quant", "moe_align", "quant_scatter",
-    "silu_mul_requant", "moe_combine", "gather_rows", "device_status", "MoELayer", "W4A8Weights", "w4a8_moe",
+    "silu_mul_requant", "moe_combine", "gather_rows", "device_status", "MoELayer", "HostPipeline", "W4A8Weights",
+    "w4a8_moe",
     "KERNEL_AUTO", "KERNEL_TC", "KERNEL_SIMT", "KERNEL_GEMV", "ops", "workloads",
 ]

@@ -159,6 +159,73 @@ class MoELayer:
     __call__ = forward
 
 
+class HostPipeline:
+    """Serves batches that live in (pinned) host memory through a layer with
+    the host<->device copies overlapped with compute.
+
+    ``submit(x, topk_ids, topk_weights, out)`` queues one batch: its inputs
+    are copied to the device on one side stream, the layer runs on the
+    caller's current stream, and its output is copied back into ``out`` on a
+    second side stream, so batch i+1's inputs and batch i-1's output move
+    while batch i computes.  Every batch's copies still happen in full; only
+    their placement in time changes.  ``depth`` device slots are recycled
+    (a slot is refilled only after its previous batch has consumed its inputs
+    and sent its output).  ``flush()`` makes the current stream wait until
+    every submitted output has reached host memory.  Works with any layer
+    whose forward is ``layer(x, topk_ids, topk_weights, out=...)``."""
+
+    def __init__(self, layer, device=None, depth: int = 2):
+        self.layer = layer
+        self.depth = depth
+        self.dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.copy_in = torch.cuda.Stream(self.dev)
+        self.copy_out = torch.cuda.Stream(self.dev)
+        self.slots = None
+        self.n = 0
+
+    def _alloc(self, x, ids, w, out):
+        def dev_like(t):
+            return torch.empty(t.shape, dtype=t.dtype, device=self.dev)
+        self.slots = [dict(x=dev_like(x), ids=dev_like(ids), w=dev_like(w), out=dev_like(out),
+                           loaded=torch.cuda.Event(), computed=torch.cuda.Event(), sent=torch.cuda.Event())
+                      for _ in range(self.depth)]
+
+    def submit(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+               out: torch.Tensor) -> None:
+        if self.slots is None or x.shape[0] > self.slots[0]["x"].shape[0]:
+            if self.slots is not None:
+                self.flush()
+            self._alloc(x, topk_ids, topk_weights, out)
+            self.n = 0
+        T = x.shape[0]
+        s = self.slots[self.n % self.depth]
+        compute = torch.cuda.current_stream(self.dev)
+        if self.n < self.depth:
+            self.copy_in.wait_stream(compute)        # nothing earlier used this slot
+        else:
+            self.copy_in.wait_event(s["computed"])   # the slot's previous batch consumed its inputs
+        with torch.cuda.stream(self.copy_in):
+            s["x"][:T].copy_(x, non_blocking=True)
+            s["ids"][:T].copy_(topk_ids, non_blocking=True)
+            s["w"][:T].copy_(topk_weights, non_blocking=True)
+            s["loaded"].record(self.copy_in)
+        compute.wait_event(s["loaded"])
+        if self.n >= self.depth:
+            compute.wait_event(s["sent"])            # the slot's previous output left the device
+        o = self.layer(s["x"][:T], s["ids"][:T], s["w"][:T], out=s["out"][:T])
+        s["computed"].record(compute)
+        self.copy_out.wait_event(s["computed"])
+        with torch.cuda.stream(self.copy_out):
+            out.copy_(o, non_blocking=True)
+            s["sent"].record(self.copy_out)
+        if o.data_ptr() != s["out"].data_ptr():      # a layer that returns its own buffer
+            o.record_stream(self.copy_out)
+        self.n += 1
+
+    def flush(self) -> None:
+        torch.cuda.current_stream(self.dev).wait_stream(self.copy_out)
+
+
 def w4a8_moe(x, topk_ids, topk_weights, w13: W4A8Weights, w2: W4A8Weights | None, group_size: int):
     """One-shot routed MoE forward (allocates its buffers; use MoELayer in a loop)."""
     layer = MoELayer(w13, w2, group_size, topk_ids.shape[1], x.shape[0])

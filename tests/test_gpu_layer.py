@@ -131,3 +131,32 @@ def test_layer_ffn_small(pkg, cuda):
     o, r = out.float(), ref.float()
     torch.testing.assert_close(o, r, rtol=0.016, atol=1e-4 * 512)
     assert (o - r).abs().mean() <= 1e-2 * r.abs().mean()
+
+
+def test_host_pipeline_matches_direct_forward(pkg, cuda):
+    """HostPipeline (copies on side streams, overlapped with compute) returns,
+    for every batch, exactly what a direct forward on device tensors returns."""
+    W = pkg.workloads
+    gen = W.make_generator(5, cuda)
+    E, H, I, gs, k = 16, 1024, 256, 128, 4
+    w13 = pkg.W4A8Weights(*W.make_int4_weights(E, 2 * I, H, gs, gen, cuda))
+    w2 = pkg.W4A8Weights(*W.make_int4_weights(E, H, I, gs, gen, cuda))
+    layer = pkg.MoELayer(w13, w2, gs, k, 64)
+    batches = []
+    for b in range(5):
+        T = 48 + 4 * b
+        x = torch.randn((T, H), generator=gen, device=cuda).to(torch.bfloat16)
+        probs = torch.softmax(torch.randn((T, E), generator=gen, device=cuda), -1)
+        tw, ids = torch.topk(probs, k, dim=-1)
+        batches.append((x, ids.to(torch.int32), (tw / tw.sum(-1, keepdim=True)).float()))
+    direct = [layer(x, ids, tw).clone() for x, ids, tw in batches]
+    pipe = pkg.HostPipeline(layer, cuda)
+    outs = []
+    for x, ids, tw in batches:
+        o = torch.empty((x.shape[0], H), dtype=torch.bfloat16).pin_memory()
+        pipe.submit(x.cpu().pin_memory(), ids.cpu().pin_memory(), tw.cpu().pin_memory(), o)
+        outs.append(o)
+    pipe.flush()
+    torch.cuda.synchronize()
+    for d, o in zip(direct, outs):
+        assert torch.equal(d.cpu(), o)
