@@ -170,7 +170,10 @@ int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_
         if (gemv_ok && M_total <= kGemvAutoRows) e = launch_gemm_gemv(a, st);
         else if (simt_ok) e = launch_gemm_simt(a, st);
         else return fail(W4A8_ERR_INVALID, "x_q rows must be at least 4-byte aligned");
-      } else if (M_total <= kGemvAutoRows) {
+      } else if (M_total <= kGemvAutoRows || M_total <= 2 * E) {
+        // at most two rows per expert on average (decode): every expert streams,
+        // one with more than kGemvMaxTokens rows in several passes, which costs
+        // less than the tensor-core launch's fixed per-K-group work
         e = launch_gemm_gemv(a, st);
       } else if (M_total >= 64 * E) {
         e = launch_gemm_tc(a, st);

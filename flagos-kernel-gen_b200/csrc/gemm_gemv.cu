@@ -184,16 +184,21 @@ __device__ __forceinline__ void partials_wrap(const uint8_t* wg, const uint8_t* 
 // GS/32 16-byte chunks (visited in a lane-rotated order, so the 16-byte
 // shared loads of a quarter warp hit distinct banks), forms the exact int32
 // partials on its own and applies w_scale; one warp reduction per token row
-// finishes the output.  NG groups of a lane are in flight at once.
-template <int R, int GS, int NG>
-__device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const TokenTile& tt, int G, int lane) {
+// finishes the output.  NG groups of a lane are in flight at once.  HALF:
+// rows with at most 16 K-groups are taken two per warp, one per half-warp
+// (`write` is false for a half-warp without a row of its own).
+template <int R, int GS, int NG, bool HALF>
+__device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const TokenTile& tt, int G, int lane,
+                                       bool write) {
   constexpr int kRot = GS == 128 ? 1 : 2;       // lane -> chunk rotation (conflict-free quarter warps)
+  constexpr int kSpan = HALF ? 16 : 32;         // lanes sharing one weight row
+  const int l = HALF ? (lane & 15) : lane;
   const int half_k = a.K >> 1;
-  const int rot = lane >> kRot;
+  const int rot = l >> kRot;
   float acc[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) acc[r] = 0.f;
-  for (int g0 = lane; g0 < G; g0 += 32 * NG) {
+  for (int g0 = l; g0 < G; g0 += kSpan * NG) {
     int g[NG], z[NG], sxv[NG][R];
     bool valid[NG];
     const uint8_t* wg[NG];
@@ -202,8 +207,8 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const
     bool any_wrap = false;
 #pragma unroll
     for (int n = 0; n < NG; ++n) {
-      valid[n] = g0 + 32 * n < G;
-      g[n] = valid[n] ? g0 + 32 * n : g0;   // an idle slot repeats the first group (result unused)
+      valid[n] = g0 + kSpan * n < G;
+      g[n] = valid[n] ? g0 + kSpan * n : g0;   // an idle slot repeats the first group (result unused)
       z[n] = j.z != nullptr ? j.z[g[n]] : a.w_zero[j.grow * G + g[n]];
       any_wrap |= z[n] < kWrapZero;
       wg[n] = j.w + g[n] * (GS / 2);
@@ -240,7 +245,8 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         acc[r] = fmaf(static_cast<float>(p[n][r]), ws, acc[r]);
-        if (a.partials != nullptr) a.partials[(static_cast<int64_t>(j.m0 + r) * a.N + j.n) * G + g[n]] = p[n][r];
+        if (a.partials != nullptr && write)
+          a.partials[(static_cast<int64_t>(j.m0 + r) * a.N + j.n) * G + g[n]] = p[n][r];
       }
     }
   }
@@ -248,8 +254,8 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const
   for (int r = 0; r < R; ++r) {
     float v = acc[r];
 #pragma unroll
-    for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
-    if (lane == 0) {
+    for (int d = kSpan / 2; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+    if (l == 0 && write) {
       const int m = j.m0 + r;
       a.out[static_cast<int64_t>(m) * a.out_stride0 + static_cast<int64_t>(j.n) * a.out_stride1] =
           __float2bfloat16_rn(v * __ldg(a.x_scale + m));
@@ -287,6 +293,77 @@ __device__ __forceinline__ void stage_tokens(const GemmArgs& a, int m0, int rows
   }
 }
 
+// Splits the tiles into gridDim.x contiguous ranges of equal cost and
+// writes this CTA's range to range[0..1].  A block of R token rows costs
+// R + 2 units (measured streaming rates at 1, 2 and 4 rows per expert are in
+// the ratio 1 : 1.34 : 2.03), so CTAs that meet multi-row experts get fewer
+// blocks and finish with the others.  Out of line, so its registers do not
+// weigh on the streaming loop.  Called by all threads (contains
+// __syncthreads); cprefix is [E+1] shared scratch.
+__device__ __noinline__ void cost_balanced_range(int E, int NB, const int* cnt, const int* prefix, int total,
+                                                  long long* cprefix, int* range) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const int per = (E + 31) / 32;
+    const int lo = lane * per;
+    long long local = 0;
+    for (int i = 0; i < per; ++i) {
+      const int e = lo + i;
+      if (e < E) {
+        const int c = cnt[e];
+        local += static_cast<long long>(NB) * (c + 2 * ((c + kGvRows - 1) / kGvRows));
+      }
+    }
+    long long incl = local;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const long long v = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += v;
+    }
+    long long run = incl - local;
+    for (int i = 0; i < per; ++i) {
+      const int e = lo + i;
+      if (e < E) {
+        cprefix[e] = run;
+        const int c = cnt[e];
+        run += static_cast<long long>(NB) * (c + 2 * ((c + kGvRows - 1) / kGvRows));
+      }
+    }
+    if (lane == 31) cprefix[E] = incl;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const long long total_cost = cprefix[E];
+    for (int side = 0; side < 2; ++side) {
+      const unsigned b = blockIdx.x + side;
+      int t;
+      if (b == 0) {
+        t = 0;
+      } else if (b == gridDim.x) {
+        t = total;
+      } else {   // first tile whose cost start is at or past the window edge
+        const long long target = total_cost * b / gridDim.x;
+        int lo = 0, hi = E - 1;
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (cprefix[mid] <= target) lo = mid; else hi = mid - 1;
+        }
+        const int tiles_e = prefix[lo + 1] - prefix[lo];
+        const long long cost_e = cprefix[lo + 1] - cprefix[lo];
+        long long local = cost_e > 0 ? ((target - cprefix[lo]) * tiles_e + cost_e - 1) / cost_e : 0;
+        if (local > tiles_e) local = tiles_e;
+        t = prefix[lo] + static_cast<int>(local);
+      }
+      range[side] = t;
+    }
+  }
+  __syncthreads();
+}
+
+// kShort: every row has at most 16 K-groups and a warp takes two rows, one
+// per half-warp (a separate instantiation, so neither mode's register
+// allocation pays for the other's code).
+template <bool kShort>
 __global__ void __launch_bounds__(kGvThreads, 2)
 gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
   extern __shared__ unsigned char smem_raw[];
@@ -314,11 +391,13 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
                 (a.N + gp.RB - 1) / gp.RB, a.min_rows, a.max_rows, true};
   const int total = sched_build(sch, a.offsets, a.M_total);   // contains __syncthreads
   const int G = a.K / a.gs;
-  // Each CTA takes a contiguous range of blocks: consecutive blocks belong to
-  // the same expert, so its token rows are staged once for many blocks.
-  const int per_cta = (total + gridDim.x - 1) / gridDim.x;
-  const int t_begin = min(total, static_cast<int>(blockIdx.x) * per_cta);
-  const int t_end = min(total, t_begin + per_cta);
+  // Each CTA takes a contiguous range of blocks (consecutive blocks belong to
+  // the same expert, so its token rows are staged once for many blocks),
+  // sized by cost rather than by count (see cost_balanced_range).
+  __shared__ int s_range[2];
+  cost_balanced_range(a.E, sch.NB, sch.cnt, sch.prefix, total,
+                      reinterpret_cast<long long*>(sched_mem + ((3 * (a.E + 1) + 1) & ~1)), s_range);
+  const int t_begin = s_range[0], t_end = s_range[1];
 
   if (warp == kGvConsumers) {
     // ------------------------------------------------------------ producer
@@ -378,23 +457,50 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
       const uint8_t* st = base + stage * stage_bytes;
       const float* s_ws = reinterpret_cast<const float*>(st + gp.stage_w);
       const int8_t* s_z = reinterpret_cast<const int8_t*>(st + gp.stage_w + gp.ws_bytes);
-      for (int rr = warp; rr < rows; rr += kGvConsumers) {
-        const RowJob job{st + rr * gp.row_bytes, gp.meta_bulk ? s_z + rr * G : nullptr,
-                         gp.meta_bulk ? s_ws + rr * G : nullptr, tile.m0, n0 + rr,
-                         static_cast<int64_t>(tile.e) * a.N + n0 + rr};
-        if (a.gs == 128) {
-          switch (tile.rows) {   // warp-uniform: the tile's token count
-            case 1: gv_row<1, 128, 2>(a, job, tt, G, lane); break;
-            case 2: gv_row<2, 128, 2>(a, job, tt, G, lane); break;
-            case 3: gv_row<3, 128, 1>(a, job, tt, G, lane); break;
-            default: gv_row<4, 128, 1>(a, job, tt, G, lane); break;
+      if constexpr (kShort) {
+        // short rows: two per warp, one per half-warp
+        for (int rr = 2 * warp; rr < rows; rr += 2 * kGvConsumers) {
+          const int mine = rr + (lane >> 4);
+          const bool write = mine < rows;
+          const int ri = write ? mine : rr;
+          const RowJob job{st + ri * gp.row_bytes, gp.meta_bulk ? s_z + ri * G : nullptr,
+                           gp.meta_bulk ? s_ws + ri * G : nullptr, tile.m0, n0 + ri,
+                           static_cast<int64_t>(tile.e) * a.N + n0 + ri};
+          if (a.gs == 128) {
+            switch (tile.rows) {   // warp-uniform: the tile's token count
+              case 1: gv_row<1, 128, 1, true>(a, job, tt, G, lane, write); break;
+              case 2: gv_row<2, 128, 1, true>(a, job, tt, G, lane, write); break;
+              case 3: gv_row<3, 128, 1, true>(a, job, tt, G, lane, write); break;
+              default: gv_row<4, 128, 1, true>(a, job, tt, G, lane, write); break;
+            }
+          } else {
+            switch (tile.rows) {
+              case 1: gv_row<1, 64, 1, true>(a, job, tt, G, lane, write); break;
+              case 2: gv_row<2, 64, 1, true>(a, job, tt, G, lane, write); break;
+              case 3: gv_row<3, 64, 1, true>(a, job, tt, G, lane, write); break;
+              default: gv_row<4, 64, 1, true>(a, job, tt, G, lane, write); break;
+            }
           }
-        } else {
-          switch (tile.rows) {
-            case 1: gv_row<1, 64, 2>(a, job, tt, G, lane); break;
-            case 2: gv_row<2, 64, 2>(a, job, tt, G, lane); break;
-            case 3: gv_row<3, 64, 1>(a, job, tt, G, lane); break;
-            default: gv_row<4, 64, 1>(a, job, tt, G, lane); break;
+        }
+      } else {
+        for (int rr = warp; rr < rows; rr += kGvConsumers) {
+          const RowJob job{st + rr * gp.row_bytes, gp.meta_bulk ? s_z + rr * G : nullptr,
+                           gp.meta_bulk ? s_ws + rr * G : nullptr, tile.m0, n0 + rr,
+                           static_cast<int64_t>(tile.e) * a.N + n0 + rr};
+          if (a.gs == 128) {
+            switch (tile.rows) {   // warp-uniform: the tile's token count
+              case 1: gv_row<1, 128, 2, false>(a, job, tt, G, lane, true); break;
+              case 2: gv_row<2, 128, 2, false>(a, job, tt, G, lane, true); break;
+              case 3: gv_row<3, 128, 1, false>(a, job, tt, G, lane, true); break;
+              default: gv_row<4, 128, 1, false>(a, job, tt, G, lane, true); break;
+            }
+          } else {
+            switch (tile.rows) {
+              case 1: gv_row<1, 64, 2, false>(a, job, tt, G, lane, true); break;
+              case 2: gv_row<2, 64, 2, false>(a, job, tt, G, lane, true); break;
+              case 3: gv_row<3, 64, 1, false>(a, job, tt, G, lane, true); break;
+              default: gv_row<4, 64, 1, false>(a, job, tt, G, lane, true); break;
+            }
           }
         }
       }
@@ -433,7 +539,8 @@ cudaError_t launch_gemm_gemv(const GemmArgs& a, cudaStream_t stream) {
   gp.x_bytes = kGvRows * a.K;                    // K is a multiple of 64: both halves stay 16-byte aligned
   gp.sx_bytes = ((kGvRows * G * 4 + 15) / 16) * 16;
   const size_t stage_bytes = gp.stage_w + gp.ws_bytes + gp.z_bytes;
-  const size_t fixed = 128 + gp.x_bytes + gp.sx_bytes + 2 * kGvMaxStages * 8 + 16 + sizeof(int) * 3 * (a.E + 1);
+  const size_t fixed = 128 + gp.x_bytes + gp.sx_bytes + 2 * kGvMaxStages * 8 + 16 + sizeof(int) * 3 * (a.E + 1) + 8 +
+                       sizeof(long long) * (a.E + 1);
   // deepest ring that keeps two CTAs per SM, else the deepest that fits one
   gp.stages = kGvMaxStages;
   while (gp.stages > 2 && fixed + gp.stages * stage_bytes > kGvSmemBudget) --gp.stages;
@@ -443,17 +550,17 @@ cudaError_t launch_gemm_gemv(const GemmArgs& a, cudaStream_t stream) {
   }
   const size_t smem = fixed + gp.stages * stage_bytes;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(gemm_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  auto kernel = G <= 16 ? gemm_gemv_kernel<true> : gemm_gemv_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_gemv_kernel, kGvThreads, smem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kGvThreads, smem);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) per_sm = 1;
-  gemm_gemv_kernel<<<sms * per_sm, kGvThreads, smem, stream>>>(a, gp);   // persistent: resident CTAs only
+  kernel<<<sms * per_sm, kGvThreads, smem, stream>>>(a, gp);   // persistent: resident CTAs only
   return cudaGetLastError();
 }
 

@@ -85,7 +85,7 @@ def gemm_auto_kernels(m_total: int, num_experts: int) -> tuple[str, ...]:
     ``m_total`` rows over ``num_experts`` experts (the host-side rule of
     ``w4a8_group_gemm_moe_ex``; the per-expert split is then made on the
     device).  Used for launch accounting and roofline labels."""
-    if m_total <= GEMV_AUTO_ROWS:
+    if m_total <= GEMV_AUTO_ROWS or m_total <= 2 * num_experts:
         return ("gemm_gemv_kernel",)
     if m_total >= 64 * num_experts:
         return ("gemm_tc_kernel",)
