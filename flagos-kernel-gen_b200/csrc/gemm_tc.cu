@@ -25,24 +25,29 @@
 //
 // Warp roles (512 threads, one CTA per SM, persistent over tiles):
 //   warp 0      TMA producer of token tiles [rows x 128 B] (128-byte swizzle)
-//   warps 1, 3  MMA issuers, one thread each, one per TMEM accumulator (warp 1
-//               also allocates TMEM)
+//   warps 1, 3  MMA issuers, one thread each, alternating K-groups between
+//               them (warp 1 also allocates TMEM)
 //   warp 2      TMA producer of packed weight tiles [128 rows x 64 B] (64-byte
 //               swizzle), running ahead on its own deeper ring
-//   warps 4-7   transform: thread r unpacks weight row r (nibble order of
-//               docs/Task1.md:78-81, zero fold with the int8 wrap of :84-85)
-//               into the canonical 128B-swizzled K-major layout the MMA reads
-//   warps 8-15  epilogue: two warpgroups of 128 token columns each; an
-//               accumulator is handed back to the MMA as soon as its last
-//               columns are in registers, before their fp32 math
+//   transform   one warpgroup (warps 4-7) or, with 64-token tiles, two
+//               taking K blocks in turn (warps 4-11): thread r unpacks weight
+//               row r (nibble order of docs/Task1.md:78-81, zero fold with the
+//               int8 wrap of :84-85) into the canonical 128B-swizzled K-major
+//               layout the MMA reads
+//   epilogue    the remaining warpgroups (warps 8-15 as two column halves,
+//               or warps 12-15); an accumulator is handed back to the MMA as
+//               soon as its last columns are in registers, before their fp32
+//               math
 //
 // The packed-weight ring is read with ordinary shared loads and refilled by
 // TMA (async proxy): a stage is released only after the unpacked bytes that
 // depend on every loaded value have been stored, so no refill can overtake
 // an outstanding read.
 //
-// Register split (setmaxnreg): warpgroups 0-1 drop to 56, the epilogue
-// warpgroups rise to 200: 2*128*56 + 2*128*200 = 65536 = the launch's 512 x 128.
+// Register split (setmaxnreg): the producer/issuer warpgroup drops to 56,
+// the transform warpgroups to 56 (one) or 64 (two), the epilogue warpgroups
+// rise to 200: 128*(56 + 56 + 2*200) = 65536 or 128*(56 + 2*64 + 200) =
+// 49152, both within the launch's 512 x 128.
 #include "common.cuh"
 #include "w4a8_internal.h"
 
@@ -54,33 +59,76 @@ namespace w4a8 {
 namespace {
 
 constexpr int kBW = 128;         // weight rows per tile (MMA M)
-constexpr int kBT = 256;         // max token rows per tile (MMA N)
 constexpr int kBK = 128;         // K bytes per pipeline stage
-constexpr int kXStages = 3;      // token tile ring
 constexpr int kWStages = 8;      // packed weight ring
-constexpr int kAStages = 2;      // unpacked weight ring
-constexpr int kXBytes = kBT * kBK;          // 32 KB
 constexpr int kABytes = kBW * kBK;          // 16 KB
 constexpr int kWBytes = kBW * (kBK / 2);    // 8 KB
 constexpr int kThreads = 512;
-constexpr int kTmemCols = 512;   // 2 accumulators x 256 columns
+constexpr int kTmemCols = 512;   // all of TMEM: kBufs accumulators x kBT columns
 constexpr int kXBoxRows = 16;
 constexpr int kMaxExperts = 1024;
 
 constexpr int kTransformWarp0 = 4;
-constexpr int kEpilogueWarp0 = 8;
-constexpr int kNumEpilogueWarps = 8;
-constexpr int kEpiCols = kBT / 2;           // columns per epilogue warpgroup
 constexpr uint32_t kMagicBits = 0x4B400000u;  // 1.5 * 2^23
 constexpr float kMagic = 12582912.0f;
 
 constexpr int kSeedBytes = 2048;   // two 1 KB swizzle atoms holding the accumulator-seed operands
-constexpr size_t kSmemTiles = size_t(kSeedBytes) + size_t(kXStages) * kXBytes + size_t(kAStages) * kABytes +
-                              size_t(kWStages) * kWBytes;
-constexpr int kNumBars = 2 * kXStages + 2 * kWStages + 2 * kAStages + 4;
 
-__host__ __device__ constexpr size_t tc_smem_bytes(int E) {
-  return 1024 /*alignment slack*/ + kSmemTiles + kNumBars * 8 + 16 + sizeof(int) * 3 * (E + 1);
+// Tile configurations.  kBT: token rows per tile (MMA N, rounded up to 16 per
+// tile at run time); kXStages / kAStages: depths of the token-tile and
+// unpacked-weight rings; kBufs: TMEM accumulators, alternating between the
+// two MMA issuers; kTransformWGs / kEpilogueWGs: warpgroups 1-3 split
+// between the int4 -> int8 transform (taking K blocks in turn) and the
+// epilogue (splitting the tile's columns).  With few tokens per tile the
+// epilogue has little to do and the per-K-group period is set by the
+// transform and by round trips through the rings, so narrower tiles trade
+// token-tile width for ring depth (and, at 64 tokens, a second transform
+// warpgroup).
+template <int BT, int XS, int AS, int NB, int TW, int TR, int ER>
+struct TcConfig {
+  static constexpr int kBT = BT;
+  static constexpr int kXStages = XS;
+  static constexpr int kAStages = AS;
+  static constexpr int kBufs = NB;
+  static constexpr int kTransformWGs = TW;
+  static constexpr int kEpilogueWGs = 3 - TW;
+  static constexpr int kEpiWarp0 = kTransformWarp0 + 4 * TW;
+  static constexpr int kEpiWarps = 4 * kEpilogueWGs;
+  static constexpr int kXBytes = BT * kBK;
+  static constexpr int kEpiCols = BT / kEpilogueWGs;   // columns per epilogue warpgroup
+  static constexpr int kTransformRegs = TR;        // setmaxnreg of the transform warpgroups
+  static constexpr int kEpilogueRegs = ER;         // setmaxnreg of the epilogue warpgroups
+  static constexpr size_t kSmemTiles =
+      size_t(kSeedBytes) + size_t(XS) * kXBytes + size_t(AS) * kABytes + size_t(kWStages) * kWBytes;
+  static constexpr int kNumBars = 2 * XS + 2 * kWStages + 2 * AS + 2 * NB;
+  static constexpr size_t smem_bytes(int E) {
+    return 1024 /*alignment slack*/ + kSmemTiles + kNumBars * 8 + 16 + sizeof(int) * 3 * (E + 1);
+  }
+  static_assert(NB % 2 == 0 && NB * BT <= kTmemCols && (TW == 1 || TW == 2) && kEpiCols % 32 == 0,
+                "tile configuration");
+  // the register split must fit the launch's 512 x 128 registers, or a
+  // setmaxnreg.inc waits forever
+  static_assert(128 * (56 + TW * TR + (3 - TW) * ER) <= kThreads * 128 && TR % 8 == 0 && ER % 8 == 0,
+                "register split");
+};
+// Three tile widths, chosen per launch by the average rows per expert
+// (measured on B200, 256 experts, N 4096, K 7168): at <= 32 rows per expert
+// the 64-token tiles with a second transform warpgroup run 1.66 ms against
+// 2.18 ms for 256-token tiles; at 128 rows the 128-token tiles run 2.27 ms
+// against 3.41 ms; from ~200 rows on the 256-token tiles are fastest.
+using TcSmall = TcConfig<64, 6, 6, 8, 2, 64, 200>;    // up to 64 tokens per tile, two transform warpgroups
+using TcMid = TcConfig<128, 4, 4, 4, 1, 56, 200>;     // up to 128 tokens per tile
+using TcWide = TcConfig<256, 3, 2, 2, 1, 56, 200>;    // up to 256 tokens per tile
+constexpr int kSmallTileAvgRows = 48;    // average rows per expert up to which TcSmall runs
+constexpr int kMidTileAvgRows = 160;     // ... and TcMid
+static_assert(TcSmall::smem_bytes(kMaxExperts) <= 227 * 1024, "small configuration exceeds shared memory");
+static_assert(TcMid::smem_bytes(kMaxExperts) <= 227 * 1024, "mid configuration exceeds shared memory");
+static_assert(TcWide::smem_bytes(kMaxExperts) <= 227 * 1024, "wide configuration exceeds shared memory");
+
+// signed byte b (0..7) of an 8-byte window
+__device__ __forceinline__ int window_byte(uint2 w, int b) {
+  const uint32_t v = b < 4 ? w.x : w.y;
+  return static_cast<int>(static_cast<int8_t>(static_cast<uint8_t>(v >> ((b & 3) * 8))));
 }
 
 __device__ __forceinline__ uint32_t pack_fold(uint32_t nib4, uint32_t c7, uint32_t c8) {
@@ -140,9 +188,13 @@ __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
   return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
 }
 
+template <class C>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                const GemmArgs a) {
+  constexpr int kBT = C::kBT, kXStages = C::kXStages, kAStages = C::kAStages, kBufs = C::kBufs;
+  constexpr int kXBytes = C::kXBytes, kEpiCols = C::kEpiCols, kEpiWarp0 = C::kEpiWarp0;
+  constexpr int kTransformWGs = C::kTransformWGs;
   extern __shared__ unsigned char smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -158,8 +210,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   uint64_t* a_full = w_empty + kWStages;
   uint64_t* a_empty = a_full + kAStages;
   uint64_t* tmem_full = a_empty + kAStages;
-  uint64_t* tmem_empty = tmem_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+  uint64_t* tmem_empty = tmem_full + kBufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + kBufs);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* sched_mem = reinterpret_cast<int*>(tmem_slot + 4);
 
@@ -180,9 +232,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
       mbar_init(&a_full[s], 4);
       mbar_init(&a_empty[s], groups_per_block);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kBufs; ++b) {
       mbar_init(&tmem_full[b], 1);
-      mbar_init(&tmem_empty[b], kNumEpilogueWarps);
+      mbar_init(&tmem_empty[b], C::kEpiWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -220,70 +272,76 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   // allocates the code that follows within that budget.
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+   // The producer and issuer warps run their loops with all 32 lanes (the
+   // waits too), and only the TMA / MMA / commit instructions sit in a short
+   // lane-0 block: a loop run by one lane of a diverged warp pays a
+   // branch-resolution stall on every branch, which measured ~20-30 cycles
+   // per instruction here and set the K-group period of small tiles.
    if (warp == 0) {
     // ------------------------------------------------------------ TMA producer: token tiles
-    if (lane == 0) {
-      const uint64_t pol_x = policy_evict_last();
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int t = blockIdx.x; t < total; t += gridDim.x) {
-        const Tile tile = sched_tile(sch, t);
-        const int nx = (tile.rows + kXBoxRows - 1) / kXBoxRows;
-        const uint32_t bytes = nx * kXBoxRows * kBK;
-        for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(&x_empty[stage], phase ^ 1, a.status, kDevTimeoutLoadEmpty, abort_flag))
-            goto x_done;
+    const uint64_t pol_x = policy_evict_last();
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const Tile tile = sched_tile(sch, t);
+      const int nx = (tile.rows + kXBoxRows - 1) / kXBoxRows;
+      const uint32_t bytes = nx * kXBoxRows * kBK;
+      for (int kb = 0; kb < KB; ++kb) {
+        if (!mbar_wait(&x_empty[stage], phase ^ 1, a.status, kDevTimeoutLoadEmpty, abort_flag))
+          goto x_done;
+        if (lane == 0) {
           mbar_arrive_expect_tx(&x_full[stage], bytes);
           for (int j = 0; j < nx; ++j)
             tma_load_2d(sX + stage * kXBytes + j * kXBoxRows * kBK, &tm_x, &x_full[stage], kb * kBK,
                         tile.m0 + j * kXBoxRows, pol_x);
-          if (++stage == kXStages) { stage = 0; phase ^= 1; }
         }
+        __syncwarp();
+        if (++stage == kXStages) { stage = 0; phase ^= 1; }
       }
-    x_done:;
     }
+  x_done:;
   } else if (warp == 2) {
     // ------------------------------------------------------------ TMA producer: packed weights
-    if (lane == 0) {
-      const uint64_t pol_keep = policy_evict_last(), pol_drop = policy_evict_first();
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int t = blockIdx.x; t < total; t += gridDim.x) {
-        const Tile tile = sched_tile(sch, t);
-        const int wrow = tile.e * a.N + tile.nb * kBW;
-        // The token blocks of one weight block run as neighbouring tiles: the
-        // earlier ones keep the weight block in L2 for the later ones, the
-        // last one lets it go.
-        const bool last_tb = tile.m0 + tile.rows >= sch.seg[tile.e] + sch.cnt[tile.e];
-        const uint64_t pol_w = last_tb ? pol_drop : pol_keep;
-        for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(&w_empty[stage], phase ^ 1, a.status, kDevTimeoutLoadEmpty, abort_flag))
-            goto w_done;
+    const uint64_t pol_keep = policy_evict_last(), pol_drop = policy_evict_first();
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const Tile tile = sched_tile(sch, t);
+      const int wrow = tile.e * a.N + tile.nb * kBW;
+      // The token blocks of one weight block run as neighbouring tiles: the
+      // earlier ones keep the weight block in L2 for the later ones, the
+      // last one lets it go.
+      const bool last_tb = tile.m0 + tile.rows >= sch.seg[tile.e] + sch.cnt[tile.e];
+      const uint64_t pol_w = last_tb ? pol_drop : pol_keep;
+      for (int kb = 0; kb < KB; ++kb) {
+        if (!mbar_wait(&w_empty[stage], phase ^ 1, a.status, kDevTimeoutLoadEmpty, abort_flag))
+          goto w_done;
+        if (lane == 0) {
           mbar_arrive_expect_tx(&w_full[stage], kWBytes);
           tma_load_2d(sW + stage * kWBytes, &tm_w, &w_full[stage], kb * (kBK / 2), wrow, pol_w);
-          if (++stage == kWStages) { stage = 0; phase ^= 1; }
         }
+        __syncwarp();
+        if (++stage == kWStages) { stage = 0; phase ^= 1; }
       }
-    w_done:;
     }
+  w_done:;
   } else if (warp == 1 || warp == 3) {
     // ------------------------------------------------------------ MMA issuers
-    // Two issuing threads, one per TMEM accumulator: thread p issues the
-    // groups c with c % 2 == p (c counts this CTA's groups), so one thread's
-    // waits and commits overlap the other's MMAs.  Each group's MMAs read one
+    // Two issuing threads: thread p issues the groups c with c % 2 == p (c
+    // counts this CTA's groups) into TMEM accumulator c % kBufs, so one
+    // thread's waits and commits overlap the other's MMAs.  Each group's MMAs read one
     // K block; its issuer commits the block's release once per group (a block
     // of two gs = 64 groups is released by both issuers; a trailing block
     // with one group is committed twice by its issuer).
-    if (lane == 0) {
+    {
       const int p = warp == 1 ? 0 : 1;
       const uint64_t desc_x0 = make_desc_sw128(smem_u32(sX));
       const uint64_t desc_a0 = make_desc_sw128(smem_u32(sA));
       constexpr uint64_t kSboMask = ~(static_cast<uint64_t>(0x3FFF) << 32);
       const uint64_t seed_a = make_desc_sw128(smem_u32(sSeed)) & kSboMask;          // row-group stride 0
       const uint64_t seed_b = make_desc_sw128(smem_u32(sSeed + 1024)) & kSboMask;
-      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(p * kBT);
       int stage = 0, astage = 0, c = 0;
-      uint32_t phase = 0, aphase = 0, bphase = 0;
+      uint32_t phase = 0, aphase = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         const Tile tile = sched_tile(sch, t);
         const int n_mma = (tile.rows + 15) & ~15;
@@ -295,24 +353,30 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
           if ((c & 1) == p) {
             if (!mbar_wait(&x_full[stage], phase, a.status, kDevTimeoutLoadFull, abort_flag)) goto mma_done;
             if (!mbar_wait(&a_full[astage], aphase, a.status, kDevTimeoutAFull, abort_flag)) goto mma_done;
-            if (!mbar_wait(&tmem_empty[p], bphase ^ 1, a.status, kDevTimeoutTmemEmpty, abort_flag))
+            const int buf = c % kBufs;
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kBT);
+            if (!mbar_wait(&tmem_empty[buf], ((c / kBufs) & 1) ^ 1, a.status, kDevTimeoutTmemEmpty, abort_flag))
               goto mma_done;
-            tc_fence_after();
             // descriptors advance by (byte offset >> 4) in their start-address field
             const uint64_t adesc = desc_a0 + static_cast<uint64_t>((astage * kABytes + sub * kpg * 32) >> 4);
             const uint64_t bdesc = desc_x0 + static_cast<uint64_t>((stage * kXBytes + sub * kpg * 32) >> 4);
-            // seed: every accumulator element = bits of 1.5 * 2^23; the int8 MMAs then add P
-            mma_bf16_ss_overwrite(d_tmem, seed_a, seed_b, idesc_seed);
-            for (int ks = 0; ks < kpg; ++ks)
-              mma_i8_ss(d_tmem, adesc + 2 * ks, bdesc + 2 * ks, idesc, 1u);
-            mma_commit(&tmem_full[p]);
-            bphase ^= 1;
-            mma_commit(&x_empty[stage]);
-            mma_commit(&a_empty[astage]);
-            if (block_end && sub + 1 < gpk) {   // a trailing block with fewer groups than its count
+            const bool trailing = block_end && sub + 1 < gpk;   // a trailing block with fewer groups than its count
+            if (lane == 0) {
+              tc_fence_after();
+              // seed: every accumulator element = bits of 1.5 * 2^23; the int8 MMAs then add P
+              mma_bf16_ss_overwrite(d_tmem, seed_a, seed_b, idesc_seed);
+#pragma unroll 4
+              for (int ks = 0; ks < kpg; ++ks)
+                mma_i8_ss(d_tmem, adesc + 2 * ks, bdesc + 2 * ks, idesc, 1u);
+              mma_commit(&tmem_full[buf]);
               mma_commit(&x_empty[stage]);
               mma_commit(&a_empty[astage]);
+              if (trailing) {
+                mma_commit(&x_empty[stage]);
+                mma_commit(&a_empty[astage]);
+              }
             }
+            __syncwarp();
           }
           if (block_end) {
             sub = 0;
@@ -326,11 +390,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     mma_done:;
     }
    }
-  } else if (warp < kEpilogueWarp0) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+  } else if (warp < kEpiWarp0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::kTransformRegs));
     // ------------------------------------------------------------ int4 -> int8 transform
-    const int r = (warp - kTransformWarp0) * 32 + lane;  // weight row within the tile
+    const int tg = (warp - kTransformWarp0) >> 2;              // transform warpgroup: K blocks kb % kTransformWGs == tg
+    const int r = ((warp - kTransformWarp0) & 3) * 32 + lane;  // weight row within the tile
     const int sw = (r >> 1) & 3;                         // 64-byte swizzle of the packed tile
+    // Zero points arrive in windows of 8 groups (one 8-byte load), the next
+    // window in flight while the current one is used: a global load's latency
+    // (the tile's zero points and scales do not stay in L1 beside this
+    // kernel's shared memory) is spread over 8 K-groups instead of stalling
+    // every one.  Rows with G % 8 != 0 load each K block's bytes when used.
+    const bool zvec = (G % 8) == 0 && (reinterpret_cast<uintptr_t>(a.w_zero) % 8) == 0;
     int stage = 0, astage = 0;
     uint32_t phase = 0, aphase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
@@ -338,16 +409,35 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
       const int n = tile.nb * kBW + r;
       const bool valid = n < a.N;
       const int8_t* zrow = a.w_zero + (static_cast<int64_t>(tile.e) * a.N + (valid ? n : 0)) * G;
-      int z0n = valid ? zrow[0] : 0;
-      int z1n = (gpk == 2 && valid && 1 < G) ? zrow[1] : z0n;
+      uint2 zw = make_uint2(0u, 0u), zw_next = make_uint2(0u, 0u);
+      int zwi = 0;   // window held in zw
+      if (zvec && valid) {
+        zw = __ldg(reinterpret_cast<const uint2*>(zrow));
+        if (G > 8) zw_next = __ldg(reinterpret_cast<const uint2*>(zrow + 8));
+      }
       for (int kb = 0; kb < KB; ++kb) {
-        const int z0 = z0n, z1 = z1n;
-        {  // prefetch the next K block's zero points
-          const int g0 = (kb + 1) * gpk;
-          if (valid && g0 < G) {
-            z0n = zrow[g0];
-            z1n = (gpk == 2 && g0 + 1 < G) ? zrow[g0 + 1] : z0n;
+        if constexpr (kTransformWGs > 1) {
+          if (kb % kTransformWGs != tg) {   // the other warpgroup's block: advance the rings only
+            if (++stage == kWStages) { stage = 0; phase ^= 1; }
+            if (++astage == kAStages) { astage = 0; aphase ^= 1; }
+            continue;
           }
+        }
+        const int g0 = kb * gpk;
+        int z0 = 0, z1 = 0;
+        if (zvec) {
+          const int b = g0 & 7;
+          if ((g0 >> 3) != zwi) {   // blocks step by at most 4 groups: windows advance one at a time
+            zw = zw_next;
+            ++zwi;
+            const int next = 8 * (zwi + 1);   // first group of the following window (8-byte aligned)
+            if (valid && next < G) zw_next = __ldg(reinterpret_cast<const uint2*>(zrow + next));
+          }
+          z0 = window_byte(zw, b);
+          z1 = gpk == 2 ? window_byte(zw, b + 1) : z0;   // gs = 64: b is even, b + 1 in the same window
+        } else if (valid) {
+          z0 = zrow[g0];
+          z1 = (gpk == 2 && g0 + 1 < G) ? zrow[g0 + 1] : z0;
         }
         if (!mbar_wait(&w_full[stage], phase, a.status, kDevTimeoutLoadFull, abort_flag)) goto tr_done;
         uint4 pk[4];
@@ -396,10 +486,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     }
   tr_done:;
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 200;");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::kEpilogueRegs));
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;                     // TMEM lane quarter this warp may access
-    const int wg = (warp - kEpilogueWarp0) >> 2;      // column half
+    const int wg = (warp - kEpiWarp0) >> 2;           // column range of this warpgroup
     const int r = quarter * 32 + lane;                // weight row within the tile
     const uint64_t magic2 = f2_pack(kMagic, kMagic);
     int buf = 0;
@@ -451,8 +541,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             }
           }
         }
-        buf ^= 1;
-        if (buf == 0) bphase ^= 1;
+        if (++buf == kBufs) { buf = 0; bphase ^= 1; }
       }
       if (valid) {
 #pragma unroll
@@ -508,6 +597,31 @@ bool encode_2d_u8(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t ou
   return r == CUDA_SUCCESS;
 }
 
+template <class C>
+cudaError_t launch_tc_config(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const GemmArgs& a,
+                             cudaStream_t stream) {
+  // The setmaxnreg split relies on the launch's 512 x 128 registers; with
+  // fewer, the epilogue's setmaxnreg.inc could wait forever, so refuse to
+  // launch.
+  static int regs_checked = 0;
+  if (!regs_checked) {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, gemm_tc_kernel<C>);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != 128) return cudaErrorInvalidConfiguration;
+    regs_checked = 1;
+  }
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const size_t smem = C::smem_bytes(a.E);
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  gemm_tc_kernel<C><<<sms, kThreads, smem, stream>>>(tm_x, tm_w, a);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_gemm_tc(const GemmArgs& a, cudaStream_t stream) {
@@ -526,26 +640,12 @@ cudaError_t launch_gemm_tc(const GemmArgs& a, cudaStream_t stream) {
                     kBK / 2, kBW, CU_TENSOR_MAP_SWIZZLE_64B))
     return cudaErrorInvalidValue;
 
-  // The setmaxnreg split (2 x 128 threads at 56 + 2 x 128 at 200 registers)
-  // needs exactly the launch's 512 x 128 registers; with fewer, the
-  // epilogue's setmaxnreg.inc would wait forever, so refuse to launch.
-  static int regs_checked = 0;
-  if (!regs_checked) {
-    cudaFuncAttributes fa;
-    cudaError_t e = cudaFuncGetAttributes(&fa, gemm_tc_kernel);
-    if (e != cudaSuccess) return e;
-    if (fa.numRegs != 128) return cudaErrorInvalidConfiguration;
-    regs_checked = 1;
-  }
-  int dev = 0, sms = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const size_t smem = tc_smem_bytes(a.E);
-  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
-  gemm_tc_kernel<<<sms, kThreads, smem, stream>>>(tm_x, tm_w, a);
-  return cudaGetLastError();
+  // Tile width by the average rows per expert (the launch's configuration is
+  // fixed on the host, without a device synchronisation).
+  const int64_t rows = a.M_total, experts = a.E;
+  if (rows <= kSmallTileAvgRows * experts) return launch_tc_config<TcSmall>(tm_x, tm_w, a, stream);
+  if (rows <= kMidTileAvgRows * experts) return launch_tc_config<TcMid>(tm_x, tm_w, a, stream);
+  return launch_tc_config<TcWide>(tm_x, tm_w, a, stream);
 }
 
 bool gemm_tc_supports(int K, int gs, int E) { return K >= kBK && K % 64 == 0 && (gs == 64 || gs == 128) && E <= kMaxExperts; }
