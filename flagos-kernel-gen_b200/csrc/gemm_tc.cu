@@ -65,7 +65,6 @@ constexpr int kABytes = kBW * kBK;          // 16 KB
 constexpr int kWBytes = kBW * (kBK / 2);    // 8 KB
 constexpr int kThreads = 512;
 constexpr int kTmemCols = 512;   // all of TMEM: kBufs accumulators x kBT columns
-constexpr int kXBoxRows = 16;
 constexpr int kMaxExperts = 1024;
 
 constexpr int kTransformWarp0 = 4;
@@ -95,6 +94,7 @@ struct TcConfig {
   static constexpr int kEpiWarp0 = kTransformWarp0 + 4 * TW;
   static constexpr int kEpiWarps = 4 * kEpilogueWGs;
   static constexpr int kXBytes = BT * kBK;
+  static constexpr int kXBoxRows = BT / 4;         // token rows per TMA box: at most 4 copies per stage
   static constexpr int kEpiCols = BT / kEpilogueWGs;   // columns per epilogue warpgroup
   static constexpr int kTransformRegs = TR;        // setmaxnreg of the transform warpgroups
   static constexpr int kEpilogueRegs = ER;         // setmaxnreg of the epilogue warpgroups
@@ -194,6 +194,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                const GemmArgs a) {
   constexpr int kBT = C::kBT, kXStages = C::kXStages, kAStages = C::kAStages, kBufs = C::kBufs;
   constexpr int kXBytes = C::kXBytes, kEpiCols = C::kEpiCols, kEpiWarp0 = C::kEpiWarp0;
+  constexpr int kXBoxRows = C::kXBoxRows;
   constexpr int kTransformWGs = C::kTransformWGs;
   extern __shared__ unsigned char smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -598,8 +599,11 @@ bool encode_2d_u8(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t ou
 }
 
 template <class C>
-cudaError_t launch_tc_config(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const GemmArgs& a,
-                             cudaStream_t stream) {
+cudaError_t launch_tc_config(const CUtensorMap& tm_w, const GemmArgs& a, cudaStream_t stream) {
+  CUtensorMap tm_x;
+  if (!encode_2d_u8(&tm_x, a.x_q, static_cast<uint64_t>(a.K), static_cast<uint64_t>(a.M_total),
+                    static_cast<uint64_t>(a.x_stride0), kBK, C::kXBoxRows, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
   // The setmaxnreg split relies on the launch's 512 x 128 registers; with
   // fewer, the epilogue's setmaxnreg.inc could wait forever, so refuse to
   // launch.
@@ -631,10 +635,7 @@ cudaError_t launch_gemm_tc(const GemmArgs& a, cudaStream_t stream) {
   if ((reinterpret_cast<uintptr_t>(a.x_q) & 15) || (a.x_stride0 % 16) ||
       (reinterpret_cast<uintptr_t>(a.w_packed) & 15))
     return cudaErrorInvalidValue;
-  CUtensorMap tm_x, tm_w;
-  if (!encode_2d_u8(&tm_x, a.x_q, static_cast<uint64_t>(a.K), static_cast<uint64_t>(a.M_total),
-                    static_cast<uint64_t>(a.x_stride0), kBK, kXBoxRows, CU_TENSOR_MAP_SWIZZLE_128B))
-    return cudaErrorInvalidValue;
+  CUtensorMap tm_w;
   if (!encode_2d_u8(&tm_w, a.w_packed, static_cast<uint64_t>(a.K / 2),
                     static_cast<uint64_t>(a.E) * static_cast<uint64_t>(a.N), static_cast<uint64_t>(a.K / 2),
                     kBK / 2, kBW, CU_TENSOR_MAP_SWIZZLE_64B))
@@ -643,9 +644,9 @@ cudaError_t launch_gemm_tc(const GemmArgs& a, cudaStream_t stream) {
   // Tile width by the average rows per expert (the launch's configuration is
   // fixed on the host, without a device synchronisation).
   const int64_t rows = a.M_total, experts = a.E;
-  if (rows <= kSmallTileAvgRows * experts) return launch_tc_config<TcSmall>(tm_x, tm_w, a, stream);
-  if (rows <= kMidTileAvgRows * experts) return launch_tc_config<TcMid>(tm_x, tm_w, a, stream);
-  return launch_tc_config<TcWide>(tm_x, tm_w, a, stream);
+  if (rows <= kSmallTileAvgRows * experts) return launch_tc_config<TcSmall>(tm_w, a, stream);
+  if (rows <= kMidTileAvgRows * experts) return launch_tc_config<TcMid>(tm_w, a, stream);
+  return launch_tc_config<TcWide>(tm_w, a, stream);
 }
 
 bool gemm_tc_supports(int K, int gs, int E) { return K >= kBK && K % 64 == 0 && (gs == 64 || gs == 128) && E <= kMaxExperts; }
