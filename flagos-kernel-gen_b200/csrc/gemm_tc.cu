@@ -83,7 +83,7 @@ constexpr int kSeedBytes = 2048;   // two 1 KB swizzle atoms holding the accumul
 // transform and by round trips through the rings, so narrower tiles trade
 // token-tile width for ring depth (and, at 64 tokens, a second transform
 // warpgroup).
-template <int BT, int XS, int AS, int NB, int TW, int TR, int ER>
+template <int BT, int XS, int AS, int NB, int TW, int TR, int ER, int XB>
 struct TcConfig {
   static constexpr int kBT = BT;
   static constexpr int kXStages = XS;
@@ -94,7 +94,10 @@ struct TcConfig {
   static constexpr int kEpiWarp0 = kTransformWarp0 + 4 * TW;
   static constexpr int kEpiWarps = 4 * kEpilogueWGs;
   static constexpr int kXBytes = BT * kBK;
-  static constexpr int kXBoxRows = BT / 4;         // token rows per TMA box: at most 4 copies per stage
+  // token rows per TMA box: a tile loads its rows rounded up to a box, so a
+  // large box over-fetches the next expert's rows at a tile's tail (for the
+  // 256-token tiles, 64-row boxes raised a launch's DRAM reads by a third)
+  static constexpr int kXBoxRows = XB;
   static constexpr int kEpiCols = BT / kEpilogueWGs;   // columns per epilogue warpgroup
   static constexpr int kTransformRegs = TR;        // setmaxnreg of the transform warpgroups
   static constexpr int kEpilogueRegs = ER;         // setmaxnreg of the epilogue warpgroups
@@ -104,7 +107,8 @@ struct TcConfig {
   static constexpr size_t smem_bytes(int E) {
     return 1024 /*alignment slack*/ + kSmemTiles + kNumBars * 8 + 16 + sizeof(int) * 3 * (E + 1);
   }
-  static_assert(NB % 2 == 0 && NB * BT <= kTmemCols && (TW == 1 || TW == 2) && kEpiCols % 32 == 0,
+  static_assert(NB % 2 == 0 && NB * BT <= kTmemCols && (TW == 1 || TW == 2) && kEpiCols % 32 == 0 &&
+                    BT % XB == 0 && XB % 8 == 0,
                 "tile configuration");
   // the register split must fit the launch's 512 x 128 registers, or a
   // setmaxnreg.inc waits forever
@@ -116,9 +120,9 @@ struct TcConfig {
 // the 64-token tiles with a second transform warpgroup run 1.66 ms against
 // 2.18 ms for 256-token tiles; at 128 rows the 128-token tiles run 2.27 ms
 // against 3.41 ms; from ~200 rows on the 256-token tiles are fastest.
-using TcSmall = TcConfig<64, 6, 6, 8, 2, 64, 200>;    // up to 64 tokens per tile, two transform warpgroups
-using TcMid = TcConfig<128, 4, 4, 4, 1, 56, 200>;     // up to 128 tokens per tile
-using TcWide = TcConfig<256, 3, 2, 2, 1, 56, 200>;    // up to 256 tokens per tile
+using TcSmall = TcConfig<64, 6, 6, 8, 2, 64, 200, 16>;    // up to 64 tokens per tile, two transform warpgroups
+using TcMid = TcConfig<128, 4, 4, 4, 1, 56, 200, 32>;     // up to 128 tokens per tile
+using TcWide = TcConfig<256, 3, 2, 2, 1, 56, 200, 16>;    // up to 256 tokens per tile
 constexpr int kSmallTileAvgRows = 48;    // average rows per expert up to which TcSmall runs
 constexpr int kMidTileAvgRows = 160;     // ... and TcMid
 static_assert(TcSmall::smem_bytes(kMaxExperts) <= 227 * 1024, "small configuration exceeds shared memory");
