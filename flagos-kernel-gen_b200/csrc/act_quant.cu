@@ -41,7 +41,9 @@ __device__ __forceinline__ int8_t quant1(float x, float s) {
 }
 
 // One CTA per token row.  rows_out: nullptr -> write row t to out row t;
-// otherwise write row t to rows_out[t*topk + j] for j in [0, topk).
+// otherwise write row t to rows_out[t*topk + j] for j in [0, topk).  On the
+// vector path each element is quantised once, into registers, and the packed
+// row is then stored to every destination.
 __global__ void __launch_bounds__(kQThreads)
 act_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride0, int H,
                  int8_t* __restrict__ q_out, int64_t q_stride0, float* __restrict__ s_out,
@@ -78,6 +80,29 @@ act_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride0, int H,
     const int64_t row = rows_out ? rows_out[static_cast<int64_t>(t) * topk + threadIdx.x] : t;
     if (row >= 0) s_out[row] = s;
   }
+  // packed int8 row in registers (vector path): 8 values per uint2
+  uint2 qv[kQMaxVec];
+  if (vec) {
+#pragma unroll
+    for (int i = 0; i < kQMaxVec; ++i) {
+      const int v = threadIdx.x + i * kQThreads;
+      if (v < nv) {
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&buf[i]);
+        uint32_t w[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float2 f0 = __bfloat1622float2(h2[2 * j]);
+          const float2 f1 = __bfloat1622float2(h2[2 * j + 1]);
+          const uint32_t b0 = static_cast<uint8_t>(quant1(f0.x, s));
+          const uint32_t b1 = static_cast<uint8_t>(quant1(f0.y, s));
+          const uint32_t b2 = static_cast<uint8_t>(quant1(f1.x, s));
+          const uint32_t b3 = static_cast<uint8_t>(quant1(f1.y, s));
+          w[j] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        }
+        qv[i] = make_uint2(w[0], w[1]);
+      }
+    }
+  }
   for (int d = 0; d < ndst; ++d) {
     const int64_t row = rows_out ? rows_out[static_cast<int64_t>(t) * topk + d] : t;
     if (row < 0) continue;  // slot routed to no local expert
@@ -86,21 +111,7 @@ act_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride0, int H,
 #pragma unroll
       for (int i = 0; i < kQMaxVec; ++i) {
         const int v = threadIdx.x + i * kQThreads;
-        if (v < nv) {
-          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&buf[i]);
-          uint32_t w[2];
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const float2 f0 = __bfloat1622float2(h2[2 * j]);
-            const float2 f1 = __bfloat1622float2(h2[2 * j + 1]);
-            const uint32_t b0 = static_cast<uint8_t>(quant1(f0.x, s));
-            const uint32_t b1 = static_cast<uint8_t>(quant1(f0.y, s));
-            const uint32_t b2 = static_cast<uint8_t>(quant1(f1.x, s));
-            const uint32_t b3 = static_cast<uint8_t>(quant1(f1.y, s));
-            w[j] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-          }
-          reinterpret_cast<uint2*>(qr)[v] = make_uint2(w[0], w[1]);
-        }
+        if (v < nv) reinterpret_cast<uint2*>(qr)[v] = qv[i];
       }
     } else {
       for (int k = threadIdx.x; k < H; k += kQThreads) qr[k] = quant1(__bfloat162float(xr[k]), s);
