@@ -63,7 +63,6 @@ constexpr int kBK = 128;         // K bytes per pipeline stage
 constexpr int kWStages = 8;      // packed weight ring
 constexpr int kABytes = kBW * kBK;          // 16 KB
 constexpr int kWBytes = kBW * (kBK / 2);    // 8 KB
-constexpr int kThreads = 512;
 constexpr int kTmemCols = 512;   // all of TMEM: kBufs accumulators x kBT columns
 constexpr int kMaxExperts = 1024;
 
@@ -83,14 +82,17 @@ constexpr int kSeedBytes = 2048;   // two 1 KB swizzle atoms holding the accumul
 // transform and by round trips through the rings, so narrower tiles trade
 // token-tile width for ring depth (and, at 64 tokens, a second transform
 // warpgroup).
-template <int BT, int XS, int AS, int NB, int TW, int TR, int ER, int XB>
+template <int BT, int XS, int AS, int NB, int TW, int EW, int TR, int ER, int XB>
 struct TcConfig {
   static constexpr int kBT = BT;
   static constexpr int kXStages = XS;
   static constexpr int kAStages = AS;
   static constexpr int kBufs = NB;
   static constexpr int kTransformWGs = TW;
-  static constexpr int kEpilogueWGs = 3 - TW;
+  static constexpr int kEpilogueWGs = EW;
+  static constexpr int kThreads = 128 * (1 + TW + EW);
+  // registers per thread at launch (one CTA per SM): the pool setmaxnreg redistributes
+  static constexpr int kLaunchRegs = (65536 / kThreads) & ~7;
   static constexpr int kEpiWarp0 = kTransformWarp0 + 4 * TW;
   static constexpr int kEpiWarps = 4 * kEpilogueWGs;
   static constexpr int kXBytes = BT * kBK;
@@ -107,12 +109,13 @@ struct TcConfig {
   static constexpr size_t smem_bytes(int E) {
     return 1024 /*alignment slack*/ + kSmemTiles + kNumBars * 8 + 16 + sizeof(int) * 3 * (E + 1);
   }
-  static_assert(NB % 2 == 0 && NB * BT <= kTmemCols && (TW == 1 || TW == 2) && kEpiCols % 32 == 0 &&
+  static_assert(NB % 2 == 0 && NB * BT <= kTmemCols && TW >= 1 && TW <= 3 && EW >= 1 && kEpiCols % 32 == 0 &&
                     BT % XB == 0 && XB % 8 == 0,
                 "tile configuration");
   // the register split must fit the launch's 512 x 128 registers, or a
   // setmaxnreg.inc waits forever
-  static_assert(128 * (56 + TW * TR + (3 - TW) * ER) <= kThreads * 128 && TR % 8 == 0 && ER % 8 == 0,
+  static_assert(128 * (56 + TW * TR + EW * ER) <= kThreads * (kLaunchRegs > 128 ? 128 : kLaunchRegs) &&
+                    TR % 8 == 0 && ER % 8 == 0,
                 "register split");
 };
 // Three tile widths, chosen per launch by the average rows per expert
@@ -120,9 +123,9 @@ struct TcConfig {
 // the 64-token tiles with a second transform warpgroup run 1.66 ms against
 // 2.18 ms for 256-token tiles; at 128 rows the 128-token tiles run 2.27 ms
 // against 3.41 ms; from ~200 rows on the 256-token tiles are fastest.
-using TcSmall = TcConfig<64, 6, 6, 8, 2, 64, 200, 16>;    // up to 64 tokens per tile, two transform warpgroups
-using TcMid = TcConfig<128, 4, 4, 4, 1, 56, 200, 32>;     // up to 128 tokens per tile
-using TcWide = TcConfig<256, 3, 2, 2, 1, 56, 200, 16>;    // up to 256 tokens per tile
+using TcSmall = TcConfig<64, 6, 6, 8, 2, 1, 64, 200, 16>;    // up to 64 tokens per tile, two transform warpgroups
+using TcMid = TcConfig<128, 4, 4, 4, 1, 2, 56, 200, 32>;     // up to 128 tokens per tile
+using TcWide = TcConfig<256, 3, 2, 2, 1, 2, 56, 200, 16>;    // up to 256 tokens per tile
 constexpr int kSmallTileAvgRows = 48;    // average rows per expert up to which TcSmall runs
 constexpr int kMidTileAvgRows = 160;     // ... and TcMid
 static_assert(TcSmall::smem_bytes(kMaxExperts) <= 227 * 1024, "small configuration exceeds shared memory");
@@ -193,7 +196,7 @@ __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
 }
 
 template <class C>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(C::kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                const GemmArgs a) {
   constexpr int kBT = C::kBT, kXStages = C::kXStages, kAStages = C::kAStages, kBufs = C::kBufs;
@@ -258,7 +261,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   // of the B atom bf16 (0.75 * 2^23, 0 x 7); a K = 16 product of them is
   // 2 * 0.75 * 2^23 = 1.5 * 2^23, written to every accumulator element by one
   // MMA whose row-group stride is 0 (all row groups read the same atom).
-  for (int i = threadIdx.x; i < kSeedBytes / 16; i += kThreads)
+  for (int i = threadIdx.x; i < kSeedBytes / 16; i += C::kThreads)
     reinterpret_cast<uint4*>(sSeed)[i] = make_uint4(i < 64 ? 0x3F80u : 0x4AC0u, 0u, 0u, 0u);
   fence_proxy_async_smem();
   TileSched sch{sched_mem, sched_mem + (a.E + 1), sched_mem + 2 * (a.E + 1), a.E, kBT,
@@ -432,7 +435,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         int z0 = 0, z1 = 0;
         if (zvec) {
           const int b = g0 & 7;
-          if ((g0 >> 3) != zwi) {   // blocks step by at most 4 groups: windows advance one at a time
+          if ((g0 >> 3) != zwi) {   // blocks step by at most 6 groups: windows advance one at a time
             zw = zw_next;
             ++zwi;
             const int next = 8 * (zwi + 1);   // first group of the following window (8-byte aligned)
@@ -616,7 +619,7 @@ cudaError_t launch_tc_config(const CUtensorMap& tm_w, const GemmArgs& a, cudaStr
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, gemm_tc_kernel<C>);
     if (e != cudaSuccess) return e;
-    if (fa.numRegs != 128) return cudaErrorInvalidConfiguration;
+    if (fa.numRegs != C::kLaunchRegs) return cudaErrorInvalidConfiguration;
     regs_checked = 1;
   }
   int dev = 0, sms = 0;
@@ -626,7 +629,7 @@ cudaError_t launch_tc_config(const CUtensorMap& tm_w, const GemmArgs& a, cudaStr
   cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  gemm_tc_kernel<C><<<sms, kThreads, smem, stream>>>(tm_x, tm_w, a);
+  gemm_tc_kernel<C><<<sms, C::kThreads, smem, stream>>>(tm_x, tm_w, a);
   return cudaGetLastError();
 }
 

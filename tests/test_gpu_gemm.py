@@ -112,6 +112,30 @@ def test_gemm_strided_operands(pkg, cuda, kernel):
     del ref_bits
 
 
+@pytest.mark.parametrize("shape,counts", [
+    ((256, 512, 128), [16, 3, 40, 5]),          # <= 48 rows per expert: 64-token tiles
+    ((256, 512, 128), [100, 129, 64, 111]),     # <= 160: 128-token tiles, a 1-row tail tile
+    ((256, 512, 128), [300, 257, 0, 511]),      # > 160: 256-token tiles, tails of 44, 1 and 255 rows
+    ((384, 1024, 64), [260, 0, 433]),           # > 160 with group size 64
+])
+def test_tc_tile_configurations(pkg, cuda, shape, counts):
+    """The tensor-core kernel's three tile widths (chosen by the average rows
+    per expert): exact int32 partials against the oracle, bf16 outputs
+    identical to the CUDA-core kernel's (same fp32 group-scale recurrence)."""
+    N, K, gs = shape
+    E = len(counts)
+    off = torch.tensor(np.concatenate([[0], np.cumsum(counts)]), dtype=torch.int32)
+    M = int(off[-1])
+    x_q, xs, w, ws, wz, _ = pkg.workloads.make_gemm_inputs(E, M, N, K, gs, seed=M, zero_mode="wrap", offsets=off)
+    out, parts = run(pkg, cuda, x_q, xs, w, ws, wz, off, gs, KERNELS["tc"])
+    simt, _ = run(pkg, cuda, x_q, xs, w, ws, wz, off, gs, KERNELS["simt"], partials=False)
+    ref, ref_parts = O.group_gemm(x_q, xs, w, ws, wz, off, torch.zeros((M, N), dtype=torch.bfloat16), gs,
+                                  with_partials=True)
+    np.testing.assert_array_equal(parts.cpu().numpy(), ref_parts)
+    np.testing.assert_array_equal(O.bf16_bits(out.cpu()), O.bf16_bits(simt.cpu()))
+    assert_gemm_close(out, ref, O.group_gemm_f64(x_q, xs, w, ws, wz, off, gs), N)
+
+
 def test_gemm_empty_inputs(pkg, cuda):
     E, N, K, gs = 4, 256, 512, 128
     _, _, w, ws, wz, _ = pkg.workloads.make_gemm_inputs(E, 8, N, K, gs, seed=0)
