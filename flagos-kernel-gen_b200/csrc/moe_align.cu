@@ -101,7 +101,42 @@ align_scan_kernel(int R, int E, int bs, int num_chunks, int32_t* __restrict__ ch
     s_cnt[e] = run;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (E <= static_cast<int>(blockDim.x)) {
+    // block-wide exclusive scan of (count, padded count), one expert per thread
+    __shared__ int s_wc[32], s_wp[32];
+    const int e = threadIdx.x, lane = e & 31, wid = e >> 5;
+    const int c = e < E ? s_cnt[e] : 0;
+    const int pc = (c + bs - 1) / bs * bs;
+    int ic = c, ip = pc;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int uc = __shfl_up_sync(0xffffffffu, ic, d), up = __shfl_up_sync(0xffffffffu, ip, d);
+      if (lane >= d) { ic += uc; ip += up; }
+    }
+    if (lane == 31) { s_wc[wid] = ic; s_wp[wid] = ip; }
+    __syncthreads();
+    if (wid == 0) {
+      const int nw = static_cast<int>(blockDim.x) >> 5;
+      int vc = lane < nw ? s_wc[lane] : 0, vp = lane < nw ? s_wp[lane] : 0;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int uc = __shfl_up_sync(0xffffffffu, vc, d), up = __shfl_up_sync(0xffffffffu, vp, d);
+        if (lane >= d) { vc += uc; vp += up; }
+      }
+      if (lane < nw) { s_wc[lane] = vc; s_wp[lane] = vp; }   // inclusive warp totals
+    }
+    __syncthreads();
+    const int bc = wid > 0 ? s_wc[wid - 1] : 0, bp = wid > 0 ? s_wp[wid - 1] : 0;
+    if (e < E) {
+      s_off[e] = bc + ic - c;
+      s_poff[e] = bp + ip - pc;
+    }
+    if (e == E - 1) {
+      s_off[E] = bc + ic;
+      s_poff[E] = bp + ip;
+      if (num_post_pad != nullptr) *num_post_pad = bp + ip;
+    }
+  } else if (threadIdx.x == 0) {
     int o = 0, p = 0;
     for (int e = 0; e < E; ++e) {
       s_off[e] = o;
@@ -120,7 +155,7 @@ align_scan_kernel(int R, int E, int bs, int num_chunks, int32_t* __restrict__ ch
   }
   const int cap = R + E * (bs - 1);
   const int nblocks = (cap + bs - 1) / bs;
-  for (int b = threadIdx.x; b < nblocks; b += blockDim.x) {
+  for (int b = threadIdx.x; block_expert != nullptr && b < nblocks; b += blockDim.x) {
     const int row = b * bs;
     int ex = -1;
     if (row < s_poff[E]) {
@@ -131,7 +166,7 @@ align_scan_kernel(int R, int E, int bs, int num_chunks, int32_t* __restrict__ ch
       }
       ex = lo;
     }
-    if (block_expert != nullptr) block_expert[b] = ex;
+    block_expert[b] = ex;
   }
   // sentinels: per-expert padding tails and everything past num_post_pad
   if (padded_ids != nullptr) {

@@ -84,7 +84,6 @@ class MoELayer:
         dev, E, H, I, k = self.device, self.E, self.H, self.I, self.topk
         self.max_tokens = max_tokens
         R = max_tokens * k
-        cap, nblk = ops.align_capacity(R, E, self.align_block)
         lib = _lib.load()
         ws_bytes = max(int(lib.w4a8_moe_align_workspace_size(max_tokens, k, E)), 4)
         self.ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
@@ -92,9 +91,6 @@ class MoELayer:
         self.offsets = torch.empty((E + 1,), **i32)
         self.sorted_ids = torch.empty((R,), **i32)
         self.inv_pos = torch.empty((R,), **i32)
-        self.padded_ids = torch.empty((cap,), **i32)
-        self.block_expert = torch.empty((nblk,), **i32)
-        self.num_post_pad = torch.empty((1,), **i32)
         self.xq = torch.empty((R, H), dtype=torch.int8, device=dev)
         self.xs = torch.empty((R,), dtype=torch.float32, device=dev)
         n13 = 2 * I if self.ffn else I
@@ -131,8 +127,8 @@ class MoELayer:
         ids = topk_ids if topk_ids.dtype == torch.int32 else topk_ids.to(torch.int32)
         ids = ids.contiguous()
         rc = lib.w4a8_moe_align(ids.data_ptr(), T, k, self.E, self.align_block, self.offsets.data_ptr(),
-                                self.sorted_ids.data_ptr(), self.inv_pos.data_ptr(), self.padded_ids.data_ptr(),
-                                self.block_expert.data_ptr(), self.num_post_pad.data_ptr(), self.ws.data_ptr(),
+                                self.sorted_ids.data_ptr(), self.inv_pos.data_ptr(), None, None, None,
+                                self.ws.data_ptr(),
                                 self.ws.numel(), stream)
         _lib.check(rc, "moe_align")
         xq, xs = self.xq[:R], self.xs[:R]
