@@ -65,6 +65,40 @@ def test_align_dropped_ids_and_block_sizes(pkg, cuda, bs):
     _check_align(pkg, cuda, torch.zeros((0, 4), dtype=torch.int32), 8, bs)
 
 
+def test_align_many_experts(pkg, cuda):
+    """More experts than the scan's 1024 threads (its serial offset path),
+    a skewed split and dropped ids."""
+    rng = np.random.default_rng(5)
+    E = 3000
+    ids = rng.zipf(1.3, size=(4000, 8)) % (E + 7) - 3   # values in [-3, E+3]: some dropped
+    _check_align(pkg, cuda, torch.from_numpy(ids.astype(np.int32)), E, 64)
+
+
+def test_align_without_padded_outputs(pkg, cuda):
+    """The routed layer asks for no padded block map (NULL padded_ids,
+    block_expert, num_post_pad): offsets, sorted ids and inverse positions
+    must equal those of the full call."""
+    c = pkg.workloads.CONFIGS["deepseek"]
+    inp = pkg.workloads.make_moe_inputs(c, 777, seed=4, weights=False)
+    ids = inp.topk_ids.to(torch.int32).contiguous().to(cuda)
+    T, k = ids.shape
+    E, R = c.experts, T * k
+    full = pkg.moe_align(ids, E, 128)
+    lib = pkg._lib.load()
+    need = lib.w4a8_moe_align_workspace_size(T, k, E)
+    ws = torch.empty((need,), dtype=torch.uint8, device=cuda)
+    off = torch.full((E + 1,), -7, dtype=torch.int32, device=cuda)
+    srt = torch.full((R,), -7, dtype=torch.int32, device=cuda)
+    inv = torch.full((R,), -7, dtype=torch.int32, device=cuda)
+    rc = lib.w4a8_moe_align(ids.data_ptr(), T, k, E, 128, off.data_ptr(), srt.data_ptr(), inv.data_ptr(),
+                            None, None, None, ws.data_ptr(), need, torch.cuda.current_stream(cuda).cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert torch.equal(off, full.expert_offsets)
+    assert torch.equal(srt, full.sorted_ids)
+    assert torch.equal(inv, full.inv_pos)
+
+
 def test_quant_scatter_and_combine(pkg, cuda):
     c = pkg.workloads.CONFIGS["deepseek"]
     T = 200
