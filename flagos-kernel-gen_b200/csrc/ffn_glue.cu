@@ -7,6 +7,8 @@
 // moe_combine: out[t, :] = bf16( sum_{j ascending} topk_w[t, j] * y[inv_pos[t*k+j], :] )
 //   with each product and each sum rounded to fp32 (no FMA contraction), so
 //   the result is bit-exact against the same loop on the CPU.
+#include <algorithm>
+
 #include "common.cuh"
 #include "w4a8_internal.h"
 
@@ -136,7 +138,9 @@ silu_mul_requant_kernel(const __nv_bfloat16* __restrict__ h, int64_t h_stride0, 
   }
 }
 
-// One CTA per token; each thread owns 8 consecutive columns (16-byte vectors).
+// One CTA per (token, column slice); each thread owns 8 consecutive columns
+// (16-byte vectors).  The column slices (gridDim.y) give a decode-sized batch
+// enough CTAs to fill the GPU.
 __global__ void __launch_bounds__(kGThreads)
 moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int64_t y_stride0, const int32_t* __restrict__ inv_pos,
                    const float* __restrict__ topk_w, int topk, int H, __nv_bfloat16* __restrict__ out,
@@ -148,7 +152,7 @@ moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int64_t y_stride0, const
   const bool vec = ((H & 7) == 0) && ((y_stride0 & 7) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0) &&
                    ((reinterpret_cast<uintptr_t>(o) & 15) == 0);
   if (vec) {
-    for (int c = threadIdx.x; c < H / 8; c += kGThreads) {
+    for (int c = blockIdx.y * kGThreads + threadIdx.x; c < H / 8; c += kGThreads * gridDim.y) {
       float acc[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.f;
@@ -172,7 +176,7 @@ moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int64_t y_stride0, const
       reinterpret_cast<uint4*>(o)[c] = r;
     }
   } else {
-    for (int c = threadIdx.x; c < H; c += kGThreads) {
+    for (int c = blockIdx.y * kGThreads + threadIdx.x; c < H; c += kGThreads * gridDim.y) {
       float acc = 0.f;
       for (int j = 0; j < topk; ++j) {
         const int p = pos[j];
@@ -239,7 +243,9 @@ cudaError_t launch_moe_combine(const __nv_bfloat16* y, int64_t y_stride0, const 
                                const float* topk_w, int T, int topk, int H, __nv_bfloat16* out,
                                int64_t out_stride0, cudaStream_t stream) {
   if (T <= 0) return cudaSuccess;
-  moe_combine_kernel<<<T, kGThreads, 0, stream>>>(y, y_stride0, inv_pos, topk_w, topk, H, out, out_stride0);
+  const int slices = std::max(1, std::min(8, (H / 8 + kGThreads - 1) / kGThreads));   // column slices per token
+  moe_combine_kernel<<<dim3(T, slices), kGThreads, 0, stream>>>(y, y_stride0, inv_pos, topk_w, topk, H, out,
+                                                                 out_stride0);
   return cudaGetLastError();
 }
 
