@@ -52,19 +52,45 @@ int cuda_fail(cudaError_t e, const char* what) {
 constexpr int kMaxDevices = 64;
 int* g_status_ptr[kMaxDevices] = {};
 std::mutex g_status_mu;
-// Makes the stream's device current in this library's runtime.  The library
-// links its own (static) CUDA runtime, whose notion of the "current device"
-// is separate from the caller's; the stream is the authoritative handle.
-cudaError_t bind_stream_device(void* stream) {
-  if (stream == nullptr) return cudaSuccess;
-  int sdev = 0, cur = 0;
-  cudaError_t e = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev);
-  if (e != cudaSuccess) return e;
-  e = cudaGetDevice(&cur);
-  if (e != cudaSuccess) return e;
-  return sdev == cur ? cudaSuccess : cudaSetDevice(sdev);
+
+// cuCtxGetDevice of the driver, resolved through the runtime (the library
+// does not link libcuda).
+using CtxGetDeviceFn = CUresult (*)(CUdevice*);
+CtxGetDeviceFn ctx_get_device_fn() {
+  static CtxGetDeviceFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetDevice", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetDeviceFn>(p);
+  });
+  return fn;
 }
 }  // namespace
+
+// Makes the caller's device current in this library's runtime.  The library
+// links its own (static) CUDA runtime, whose "current device" is separate
+// from the caller's runtime (torch's, for example).  A stream names its
+// device; for the NULL stream the device is that of the driver context
+// current on the calling thread, which is the context the caller's runtime
+// made current with cudaSetDevice / torch.cuda.set_device and its first CUDA
+// call.  With no current context the library's own current device is kept.
+cudaError_t bind_stream_device(void* stream) {
+  int want = -1, cur = 0;
+  if (stream != nullptr) {
+    cudaError_t e = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &want);
+    if (e != cudaSuccess) return e;
+  } else if (CtxGetDeviceFn fn = ctx_get_device_fn(); fn != nullptr) {
+    CUdevice d = 0;
+    if (fn(&d) == CUDA_SUCCESS) want = static_cast<int>(d);
+  }
+  if (want < 0) return cudaSuccess;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (e != cudaSuccess) return e;
+  return want == cur ? cudaSuccess : cudaSetDevice(want);
+}
 
 void set_last_error(const char* msg) { g_last_error = msg; }
 
@@ -236,9 +262,12 @@ int w4a8_moe_align(const int32_t* topk_ids, int64_t T, int64_t topk, int64_t E, 
                    int32_t* block_expert, int32_t* num_post_pad, void* workspace, size_t workspace_bytes,
                    void* stream) {
   if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
-  if (T < 0 || topk <= 0 || E <= 0 || E > 8192 || block_size <= 0 || T * topk > INT32_MAX / 2)
-    return fail(W4A8_ERR_INVALID, "bad sizes T=%lld topk=%lld E=%lld block_size=%lld", (long long)T,
-                (long long)topk, (long long)E, (long long)block_size);
+  if (T < 0 || topk <= 0 || E <= 0 || E > 8192 || block_size <= 0 || block_size > kMaxAlignBlock ||
+      T * topk > INT32_MAX / 2 || T * topk + E * (block_size - 1) > INT32_MAX / 2)
+    return fail(W4A8_ERR_INVALID,
+                "bad sizes T=%lld topk=%lld E=%lld block_size=%lld (block_size <= %d, T*topk + E*(block_size-1) "
+                "must fit the 32-bit padded index range)",
+                (long long)T, (long long)topk, (long long)E, (long long)block_size, kMaxAlignBlock);
   if (expert_offsets == nullptr || (T > 0 && (topk_ids == nullptr || sorted_ids == nullptr || inv_pos == nullptr)))
     return fail(W4A8_ERR_INVALID, "null pointer");
   const size_t need = w4a8_moe_align_workspace_size(T, topk, E);

@@ -48,16 +48,15 @@ void* g_scratch_ptr[kMaxDevices] = {};
 std::mutex g_scratch_mu;
 
 // Device address of the scratch array on the stream's device (the symbol's
-// host-side name is not a device address).
+// host-side name is not a device address).  For the NULL stream the device is
+// that of the driver context current on the calling thread (as for every
+// entry point of the library).
 cudaError_t scratch_for(void* stream, void** out) {
-  int dev = 0;
-  cudaError_t e = stream != nullptr ? cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &dev)
-                                    : cudaGetDevice(&dev);
+  cudaError_t e = w4a8::bind_stream_device(stream);
   if (e != cudaSuccess) return e;
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  int cur = 0;
-  if ((e = cudaGetDevice(&cur)) != cudaSuccess) return e;
-  if (cur != dev && (e = cudaSetDevice(dev)) != cudaSuccess) return e;
   std::lock_guard<std::mutex> lk(g_scratch_mu);
   if (g_scratch_ptr[dev] == nullptr) {
     void* p = nullptr;
@@ -81,8 +80,8 @@ extern "C" {
 int w4a8_moe_align_noalloc(const int32_t* topk_ids, int64_t T, int64_t topk, int64_t E, int64_t block_size,
                            int32_t* expert_offsets, int32_t* sorted_ids, int32_t* inv_pos,
                            int32_t* padded_ids, int32_t* block_expert, int32_t* num_post_pad, void* stream) {
-  if (T < 0 || topk <= 0 || E <= 0 || block_size <= 0)
-    return noalloc_fail("w4a8_moe_align_noalloc: bad sizes");
+  if (T < 0 || topk <= 0 || E <= 0 || block_size <= 0 || block_size > w4a8::kMaxAlignBlock)
+    return noalloc_fail("w4a8_moe_align_noalloc: bad sizes (block_size must be in [1, 4096])");
   if (T * topk > kNoAllocMaxSlots || E > kNoAllocMaxExperts)
     return noalloc_fail("w4a8_moe_align_noalloc: T*topk must be <= 131072 and E <= 512 (fixed scratch size); "
                         "use w4a8_moe_align with a caller workspace for larger problems");

@@ -37,4 +37,13 @@ bool gemm_tc_supports(int K, int gs, int E);
 
 int* device_status_ptr();  // per-device status word (static __device__ storage)
 
+// Makes the device of `stream` (for NULL: of the driver context current on
+// the calling thread) current in the library's own runtime.
+cudaError_t bind_stream_device(void* stream);
+
+// Largest padded-block size the align entry points accept: the padded
+// outputs hold T*topk + E*(block_size-1) entries, which must stay well inside
+// the kernels' 32-bit index range.
+constexpr int kMaxAlignBlock = 4096;
+
 }  // namespace w4a8

@@ -2,8 +2,12 @@
  * w4a8moe.h -- C ABI of the B200 (sm_100a) W4A8 Mixture-of-Experts library.
  *
  * Plain pointers, sizes and strides; every pointer is CUDA device memory on
- * the current device unless stated otherwise; `stream` is a cudaStream_t
- * (NULL = legacy default stream).  Nothing here allocates device memory:
+ * the stream's device unless stated otherwise; `stream` is a cudaStream_t.
+ * The library links its own CUDA runtime: it runs each call on the device of
+ * `stream`, and for a NULL stream (the legacy default stream) on the device
+ * of the driver context current on the calling thread, i.e. the device the
+ * caller selected with cudaSetDevice (torch.cuda.set_device) and has used
+ * since.  Nothing here allocates device memory:
  * scratch space is passed in by the caller.  No call synchronises the host
  * except w4a8_device_status().
  *
@@ -113,6 +117,8 @@ size_t w4a8_moe_align_workspace_size(int64_t T, int64_t topk, int64_t E);
  *   block_expert   int32 [ceil((T*topk + E*(block_size-1)) / block_size)] or NULL (-1 past the end)
  *   num_post_pad   int32 [1] or NULL
  *   workspace      >= w4a8_moe_align_workspace_size(T, topk, E) bytes
+ * block_size is 1..4096 and T*topk + E*(block_size-1) must be below 2^30;
+ * other values return W4A8_ERR_INVALID.
  */
 int w4a8_moe_align(const int32_t* topk_ids, int64_t T, int64_t topk, int64_t E, int64_t block_size,
                    int32_t* expert_offsets, int32_t* sorted_ids, int32_t* inv_pos,
@@ -154,7 +160,8 @@ int w4a8_gather_rows(const void* src, int64_t src_stride_bytes, const int32_t* i
  * counterpart in the reference.  Same outputs as w4a8_moe_align (bit for
  * bit); its scratch is a fixed 660 KB array in the library's device memory,
  * held by every GPU that loads the library until the process exits.
- * Limits: T*topk <= 131072 and E <= 512, else W4A8_ERR_INVALID with a message.
+ * Limits: T*topk <= 131072, E <= 512 and block_size <= 4096, else
+ * W4A8_ERR_INVALID with a message.
  * Allocates nothing.  All calls share the array: calls that overlap on the GPU
  * race, so serialise them.  The first call on a device resolves the array's
  * device address; make it before capturing a stream.

@@ -3,7 +3,8 @@ own PyTorch implementations (read from the reference checkout, executed here
 on the CPU).  It needs the reference tree, so it runs only where that tree is
 mounted; the fixtures it writes are committed and travel instead.
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference-checkout
+    (or set W4A8_REFERENCE_ROOT and omit the argument)
 
 Sources executed:
   * docs/Task1.md:49-115  -- ``w4a8_group_gemm_moe`` (the operator contract).
@@ -159,4 +160,7 @@ def main(ref_root: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("W4A8_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py <reference checkout> (or set W4A8_REFERENCE_ROOT)")
+    main(root)

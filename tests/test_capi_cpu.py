@@ -70,6 +70,35 @@ def test_capi_rejects_bad_arguments_without_a_gpu(pkg):
     assert b"workspace" in lib.w4a8_last_error() or b"null" in lib.w4a8_last_error()
 
 
+@pytest.mark.parametrize("bs", [0, -3, 4097, 1 << 31, (1 << 32) + 128])
+def test_align_rejects_block_sizes_outside_the_index_range(pkg, bs):
+    """block_size is bounded in both align entry points: a value that would
+    truncate in a 32-bit cast, or make the padded index range overflow, is an
+    argument error and no kernel is launched (no GPU is touched here)."""
+    from importlib import import_module
+    L = import_module("flagos-kernel-gen_b200._lib")
+    lib = L.load()
+    p = 1 << 20
+    assert lib.w4a8_moe_align(p, 16, 8, 256, bs, p, p, p, None, None, None, p, 1 << 30, None) == L.W4A8_ERR_INVALID
+    assert b"block_size" in lib.w4a8_last_error()
+    assert lib.w4a8_moe_align_noalloc(p, 16, 8, 256, bs, p, p, p, None, None, None, None) == L.W4A8_ERR_INVALID
+    assert b"block_size" in lib.w4a8_last_error()
+
+
+def test_align_rejects_padded_range_overflow(pkg):
+    """T*topk + E*(block_size-1) beyond the 32-bit padded index range."""
+    from importlib import import_module
+    L = import_module("flagos-kernel-gen_b200._lib")
+    lib = L.load()
+    p = 1 << 20
+    # T*topk = 2^30 - 2^20 slots is accepted on its own, but 8192 experts x 4095
+    # padding entries (33.5 M) push the padded range past 2^30
+    T = (1 << 24) - (1 << 14)
+    assert lib.w4a8_moe_align(p, T, 64, 8192, 4096, p, p, p, None, None, None, p, 1 << 40, None) \
+        == L.W4A8_ERR_INVALID
+    assert b"block_size" in lib.w4a8_last_error()
+
+
 def test_python_signature_matches_reference(pkg):
     sig = inspect.signature(pkg.w4a8_group_gemm_moe)
     assert list(sig.parameters) == ["x_q", "x_scale", "w_q4_packed", "w_scale", "w_zero", "expert_offsets", "out",

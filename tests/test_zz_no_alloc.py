@@ -54,6 +54,28 @@ def test_noalloc_align_matches_workspace_align_twice(cuda):
         torch.cuda.synchronize()
         for key in ref:
             assert torch.equal(got[key], ref[key]), f"{name}: {key} differs"
+    # the documented maximum (T*topk = 131072 slots over E = 512 experts, which
+    # fills almost all of the fixed scratch), then a call that asks for no
+    # padded outputs (padded_ids, block_expert, num_post_pad = NULL)
+    T, k, E, bs = 16384, 8, 512, 128
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(3)
+    ids = torch.randint(0, E, (T, k), generator=gen, device=cuda, dtype=torch.int32)
+    ws = torch.empty((lib.w4a8_moe_align_workspace_size(T, k, E),), dtype=torch.uint8, device=cuda)
+    ref = _outputs(T * k, E, bs, cuda)
+    got = _outputs(T * k, E, bs, cuda)
+    assert _call(lib, ids, E, bs, ref, stream, workspace=ws) == L.W4A8_OK, lib.w4a8_last_error()
+    assert _call(lib, ids, E, bs, got, stream) == L.W4A8_OK, lib.w4a8_last_error()
+    torch.cuda.synchronize()
+    for key in ref:
+        assert torch.equal(got[key], ref[key]), f"maximum size: {key} differs"
+    part = _outputs(T * k, E, bs, cuda)
+    rc = lib.w4a8_moe_align_noalloc(ids.data_ptr(), T, k, E, bs, part["off"].data_ptr(), part["sorted"].data_ptr(),
+                                    part["inv"].data_ptr(), None, None, None, stream)
+    assert rc == L.W4A8_OK, lib.w4a8_last_error()
+    torch.cuda.synchronize()
+    for key in ("off", "sorted", "inv"):
+        assert torch.equal(part[key], ref[key]), f"without padded outputs: {key} differs"
     # beyond the fixed scratch size: a clear error, and nothing launched
     big = torch.zeros((16385, 8), dtype=torch.int32, device=cuda)
     o = _outputs(8, 8, 1, cuda)
