@@ -104,6 +104,8 @@ class ExpertParallelMoE:
         dev = x.device
         ops = self.ops
         g0 = getattr(ops, "gemm_launches", 0)
+        ev = _events(events)
+        ev.start("dispatch_prep")
         ids = topk_ids.to(torch.int32)
         # 1. destination rank of every slot; ids outside [0, E) are dropped (-1)
         dest = torch.where((ids >= 0) & (ids < self.E), ids // self.epr, torch.full_like(ids, -1))
@@ -111,7 +113,9 @@ class ExpertParallelMoE:
         # 2. quantise once, rows in destination order
         xq_send, xs_send = ops.quant_scatter(x, send_inv, k)
         lid_send = (ids.reshape(-1)[send_sorted.long()] % self.epr).to(torch.int32)
+        ev.stop()
         # 3. exchange counts, then rows / scales / local expert ids
+        ev.start("a2a_counts")
         send_counts = (send_off[1:] - send_off[:-1]).to(torch.int64)
         recv_counts = torch.empty_like(send_counts)
         self._a2a(recv_counts, send_counts, None, None)
@@ -123,10 +127,14 @@ class ExpertParallelMoE:
         xq_recv = torch.empty((n_recv, H), dtype=torch.int8, device=dev)
         xs_recv = torch.empty((n_recv,), dtype=torch.float32, device=dev)
         lid_recv = torch.empty((n_recv,), dtype=torch.int32, device=dev)
+        ev.stop()
+        ev.start("a2a_dispatch")
         self._a2a(xq_recv, xq_send[:n_send], out_splits, in_splits)
         self._a2a(xs_recv, xs_send[:n_send], out_splits, in_splits)
         self._a2a(lid_recv, lid_send[:n_send], out_splits, in_splits)
+        ev.stop()
         # 4. local expert order
+        ev.start("local_align_gather")
         loc_off, loc_sorted, loc_inv = ops.align(lid_recv.view(-1, 1), self.epr)
         self.offsets = loc_off
         xq_loc = ops.gather_rows(xq_recv, loc_sorted)
@@ -134,12 +142,14 @@ class ExpertParallelMoE:
         # 5. local grouped GEMMs
         n13 = self.w13.packed.shape[1]
         h = torch.empty((n_recv, n13), dtype=torch.bfloat16, device=dev)
-        ev = _events(events)
+        ev.stop()
         ev.start("gemm_gate_up")
         ops.grouped_gemm(xq_loc, xs_loc, self.w13, loc_off, h, self.gs)
         ev.stop()
         if self.w2 is not None:
+            ev.start("silu_mul_requant")
             aq, as_ = ops.silu_mul_requant(h)
+            ev.stop()
             y_loc = torch.empty((n_recv, H), dtype=torch.bfloat16, device=dev)
             ev.start("gemm_down")
             ops.grouped_gemm(aq, as_, self.w2, loc_off, y_loc, self.gs)
@@ -147,15 +157,22 @@ class ExpertParallelMoE:
         else:
             y_loc = h
         # 6. back to arrival order, then home
+        ev.start("gather_back")
         y_recv = ops.gather_rows(y_loc, loc_inv)
         y_home = torch.empty((n_send, y_loc.shape[1]), dtype=torch.bfloat16, device=dev)
+        ev.stop()
+        ev.start("a2a_combine")
         self._a2a(y_home, y_recv, in_splits, out_splits)
+        ev.stop()
         # 7. combine in token order
+        ev.start("combine")
         y_full = y_home
         if n_send < T * k:   # dropped slots have inv = -1 and are never read
             y_full = torch.empty((T * k, y_home.shape[1]), dtype=torch.bfloat16, device=dev)
             y_full[:n_send] = y_home
         self.out = ops.combine(y_full, send_inv, topk_weights)
+        ev.stop()
+        self.n_recv = n_recv
         self._last_gemm_launches = getattr(ops, "gemm_launches", 0) - g0
         return self.out
 

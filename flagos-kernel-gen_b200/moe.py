@@ -112,8 +112,9 @@ class MoELayer:
     def forward(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
                 out: torch.Tensor | None = None, events: list | None = None) -> torch.Tensor:
         """Routed forward.  ``events``: optional list; when given, (name, start,
-        end) CUDA-event pairs recorded on the current stream around each grouped
-        GEMM are appended to it (used for per-kernel timing)."""
+        end) CUDA-event pairs recorded on the current stream around each stage
+        (align, quant_scatter, gemm_gate_up, silu_mul_requant, gemm_down,
+        combine) are appended to it (used for per-stage timing)."""
         T, H = x.shape
         if T > self.max_tokens:
             self._alloc(T)
@@ -124,6 +125,8 @@ class MoELayer:
         dev = x.device
         lib = _lib.load()
         stream = torch.cuda.current_stream(dev).cuda_stream
+        ev = _Ev(events)
+        ev.start("align")
         ids = topk_ids if topk_ids.dtype == torch.int32 else topk_ids.to(torch.int32)
         ids = ids.contiguous()
         rc = lib.w4a8_moe_align(ids.data_ptr(), T, k, self.E, self.align_block, self.offsets.data_ptr(),
@@ -131,16 +134,20 @@ class MoELayer:
                                 self.ws.data_ptr(),
                                 self.ws.numel(), stream)
         _lib.check(rc, "moe_align")
+        ev.stop()
         xq, xs = self.xq[:R], self.xs[:R]
+        ev.start("quant_scatter")
         ops.quant_scatter(x, self.inv_pos[:R], k, xq, xs)
+        ev.stop()
         h = self.h[:R]
-        ev = _Ev(events)
         ev.start("gemm_gate_up")
         ops.w4a8_group_gemm_moe(xq, xs, self.w13.packed, self.w13.scale, self.w13.zero, self.offsets, h, self.gs)
         ev.stop()
         if self.ffn:
             aq, as_ = self.aq[:R], self.as_[:R]
+            ev.start("silu_mul_requant")
             ops.silu_mul_requant(h, aq, as_)
+            ev.stop()
             y = self.y[:R]
             ev.start("gemm_down")
             ops.w4a8_group_gemm_moe(aq, as_, self.w2.packed, self.w2.scale, self.w2.zero, self.offsets, y,
@@ -150,7 +157,10 @@ class MoELayer:
             y = h
         if out is None:
             out = self.out[:T]
-        return ops.moe_combine(y, self.inv_pos[:R], topk_weights, out)
+        ev.start("combine")
+        out = ops.moe_combine(y, self.inv_pos[:R], topk_weights, out)
+        ev.stop()
+        return out
 
     __call__ = forward
 

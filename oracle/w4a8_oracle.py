@@ -55,7 +55,16 @@ def fold_zero(w_int4: np.ndarray, w_zero, group_size: int) -> np.ndarray:
 
 
 def signed_weights(w_q4_packed, w_zero, group_size: int) -> np.ndarray:
-    return fold_zero(unpack_int4(w_q4_packed), w_zero, group_size)
+    """int8(nibble - zero) [..., K]: ``unpack_int4`` then ``fold_zero``, written
+    with the reference's own torch operations (nibbles widened to int16, the
+    per-group zero subtracted, ``.to(torch.int8)`` wrapping;
+    docs/Task1.md:78-85) because they run multi-threaded: ten times faster
+    than the numpy pair on the multi-GB expert tensors of the large configs.
+    The golden tests check both forms against the reference bit for bit."""
+    p = _t(w_q4_packed).to(torch.uint8)
+    nib = torch.stack([p & 0x0F, p >> 4], dim=-1).reshape(*p.shape[:-1], p.shape[-1] * 2)
+    z = _t(w_zero).to(torch.int16).repeat_interleave(group_size, dim=-1)
+    return (nib.to(torch.int16) - z).to(torch.int8).numpy()
 
 
 # ----------------------------------------------------------------------------- grouped GEMM
@@ -271,3 +280,33 @@ def error_stats(out_bf16: torch.Tensor, ref64: np.ndarray) -> dict:
                 mean_abs=float(np.abs(o - r).mean()) if r.size else 0.0,
                 bf16_floor_mean_abs=float(np.abs(r_bf - r).mean()) if r.size else 0.0,
                 mean_abs_ref=float(np.abs(r).mean()) if r.size else 0.0)
+
+
+def moe_layer_tokens(x_bf16: torch.Tensor, topk_ids, topk_w, w13, w2, group_size: int, tokens,
+                     block_size: int = 128) -> torch.Tensor:
+    """``moe_layer`` for the tokens listed in ``tokens`` only (rows in that order).
+
+    A token's output depends only on its own activations, its k (expert,
+    weight) pairs and those experts' weights: the other tokens change only the
+    order of rows inside an expert segment, and every row of the reference
+    GEMM is computed on its own.  So the layer restricted to a token subset,
+    with the experts that subset uses renumbered densely, gives the same
+    output rows.  ``w13`` / ``w2`` may live on any device; only the used
+    experts' slices are copied to the CPU, which keeps full-size checks of the
+    large configurations (GBs of expert weights) cheap."""
+    sel = torch.as_tensor(tokens, dtype=torch.long)
+    ids = _t(topk_ids).cpu().to(torch.int64)[sel]
+    E = w13[0].shape[0]
+    ok = (ids >= 0) & (ids < E)
+    used = torch.unique(ids[ok])
+    remap = torch.full((E,), -1, dtype=torch.int64)
+    remap[used] = torch.arange(used.numel())
+    ids_c = torch.where(ok, remap[ids.clamp(0, E - 1)], torch.full_like(ids, -1)).to(torch.int32)
+
+    def take(w):
+        if w is None:
+            return None
+        idx = used.to(w[0].device)
+        return tuple(t.index_select(0, idx).cpu() for t in w)
+
+    return moe_layer(x_bf16.cpu()[sel], ids_c, _t(topk_w).cpu()[sel], take(w13), take(w2), group_size, block_size)

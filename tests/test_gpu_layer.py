@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import O
+from gpu_util import O, assert_layer_close
 
 pytestmark = pytest.mark.gpu
 
@@ -162,9 +162,7 @@ def test_layer_ffn_small(pkg, cuda):
         out, ref, layer, inter = _layer_case(pkg, cuda, "_test_ffn", 96, 3)
     finally:
         del W.CONFIGS["_test_ffn"]
-    o, r = out.float(), ref.float()
-    torch.testing.assert_close(o, r, rtol=0.016, atol=1e-4 * 512)
-    assert (o - r).abs().mean() <= 1e-2 * r.abs().mean()
+    assert_layer_close(out, ref, 512, "small FFN")
 
 
 def test_host_pipeline_matches_direct_forward(pkg, cuda):

@@ -36,6 +36,16 @@ def test_exact_partials_restatement(O, golden, name):
         np.testing.assert_array_equal(p, g["partials"][m0:m1])
 
 
+@pytest.mark.parametrize("name", GEMM_CASES)
+def test_signed_weights_equal_numpy_unpack_and_fold(O, golden, name):
+    """The torch form of ``signed_weights`` equals the numpy ``unpack_int4`` +
+    ``fold_zero`` pair bit for bit (zero-point wrap included)."""
+    g = golden(name)
+    gs = int(g["gs"])
+    np.testing.assert_array_equal(O.signed_weights(g["packed"], g["zero"], gs),
+                                  O.fold_zero(O.unpack_int4(g["packed"]), g["zero"], gs))
+
+
 def test_zero_wrap_case_really_wraps(O, golden):
     g = golden("gemm_zero_wrap")
     nib = O.unpack_int4(g["packed"]).astype(np.int32)

@@ -91,3 +91,19 @@ def test_zipf_routing_is_skewed(pkg):
     inp = W.make_moe_inputs(cfg, 1024, seed=0, weights=False)
     counts = np.bincount(inp.topk_ids.numpy().reshape(-1), minlength=cfg.experts)
     assert counts.max() > 10 * np.median(counts)
+
+
+@pytest.mark.parametrize("seed,zipf", [(3, 1.2), (4, 0.0)])
+def test_layer_on_a_token_subset_equals_the_full_layer(pkg, O, seed, zipf):
+    """``moe_layer_tokens`` (used to check full-size layers on sampled
+    tokens) gives exactly the full layer's rows for those tokens, with dropped
+    slots and experts the subset does not use."""
+    W = pkg.workloads
+    cfg = W.MoEConfig("t", hidden=512, inter=256, experts=16, topk=4, zipf=zipf)
+    inp = W.make_moe_inputs(cfg, 64, seed=seed, zero_mode="random")
+    ids = inp.topk_ids.clone()
+    ids[7, 1] = -1                     # a dropped slot
+    full = O.moe_layer(inp.x, ids, inp.topk_weights, inp.w13, inp.w2, 128)
+    toks = [5, 0, 63, 7, 17]
+    sub = O.moe_layer_tokens(inp.x, ids, inp.topk_weights, inp.w13, inp.w2, 128, toks)
+    np.testing.assert_array_equal(O.bf16_bits(full[toks]), O.bf16_bits(sub))
