@@ -13,6 +13,7 @@ from .ops import (  # noqa: F401
     AlignResult,
     act_quant,
     align_capacity,
+    combine_finish,
     device_status,
     gather_rows,
     moe_align,
@@ -20,6 +21,7 @@ from .ops import (  # noqa: F401
     quant_scatter,
     silu_mul_requant,
     w4a8_group_gemm_moe,
+    w4a8_group_gemm_moe_combine,
     w4a8_group_gemm_moe_ex,
 )
 from .moe import HostPipeline, MoELayer, W4A8Weights, w4a8_moe  # noqa: F401
@@ -27,7 +29,7 @@ from ._lib import KERNEL_AUTO, KERNEL_GEMV, KERNEL_SIMT, KERNEL_TC  # noqa: F401
 from . import ops, workloads  # noqa: F401
 
 __all__ = [
-    "w4a8_group_gemm_moe", "w4a8_group_gemm_moe_ex", "act_quant", "moe_align", "quant_scatter",
+    "w4a8_group_gemm_moe", "w4a8_group_gemm_moe_ex", "w4a8_group_gemm_moe_combine", "combine_finish", "act_quant", "moe_align", "quant_scatter",
     "silu_mul_requant", "moe_combine", "gather_rows", "device_status", "MoELayer", "HostPipeline", "W4A8Weights",
     "w4a8_moe",
     "KERNEL_AUTO", "KERNEL_TC", "KERNEL_SIMT", "KERNEL_GEMV", "ops", "workloads",

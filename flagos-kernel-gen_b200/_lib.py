@@ -36,6 +36,9 @@ SIGNATURES = {
                                            _i64, _i64, _p]),
     "w4a8_group_gemm_moe_ex": (ctypes.c_int, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
                                               _i64, _i64, _i64, _i32, _p, _p]),
+    "w4a8_group_gemm_moe_combine": (ctypes.c_int, [_p, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _i64, _i64,
+                                                   _i64, _i64, _i64, _i64, _i32, _p]),
+    "w4a8_combine_finish": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _i64, _p]),
     "w4a8_act_quant": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "w4a8_quant_scatter": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _i64, _p, _p, _p]),
     "w4a8_moe_align_workspace_size": (_sz, [_i64, _i64, _i64]),
@@ -44,6 +47,7 @@ SIGNATURES = {
     "w4a8_moe_combine": (ctypes.c_int, [_p, _i64, _p, _p, _i64, _i64, _i64, _p, _i64, _p]),
     "w4a8_gather_rows": (ctypes.c_int, [_p, _i64, _p, _i64, _i64, _p, _i64, _p]),
     "w4a8_moe_align_noalloc": (ctypes.c_int, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p]),
+    "w4a8_selftest_wait_timeout": (ctypes.c_int, [_i64, _p, _p]),
     "w4a8_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32), _i32, _p]),
 }
 

@@ -28,6 +28,7 @@ SOURCES = [
     "gemm_tc.cu",
     "gemm_gemv.cu",
     "noalloc.cu",
+    "health.cu",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

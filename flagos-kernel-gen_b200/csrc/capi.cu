@@ -28,6 +28,8 @@ cudaError_t launch_gather_rows(const void* src, int64_t src_stride, const int32_
 cudaError_t launch_moe_combine(const __nv_bfloat16* y, int64_t y_stride0, const int32_t* inv_pos,
                                const float* topk_w, int T, int topk, int H, __nv_bfloat16* out,
                                int64_t out_stride0, cudaStream_t stream);
+cudaError_t launch_combine_finish(float* acc, int64_t acc_stride0, int T, int H, __nv_bfloat16* out,
+                                  int64_t out_stride0, cudaStream_t stream);
 
 namespace {
 __device__ int g_status_word;
@@ -110,18 +112,12 @@ int* device_status_ptr() {
 
 using namespace w4a8;
 
-extern "C" {
-
-int w4a8_abi_version(void) { return 1; }
-
-const char* w4a8_last_error(void) { return g_last_error.c_str(); }
-
-int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
-                           const uint8_t* w_q4_packed, const float* w_scale, const int8_t* w_zero,
-                           const int32_t* expert_offsets, void* out, int64_t out_stride0,
-                           int64_t out_stride1, int64_t M_total, int64_t E, int64_t N, int64_t K,
-                           int64_t group_size, int32_t kernel, int32_t* partials, void* stream) {
-  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+namespace {
+// Validation shared by the grouped-GEMM entry points and the argument block;
+// returns W4A8_OK with *a filled in, or an error code.
+int gemm_setup(GemmArgs* a, const int8_t* x_q, int64_t x_stride0, const float* x_scale, const uint8_t* w_q4_packed,
+               const float* w_scale, const int8_t* w_zero, const int32_t* expert_offsets, int64_t M_total,
+               int64_t E, int64_t N, int64_t K, int64_t group_size, int32_t kernel, bool need_out, void* out) {
   if (group_size != 64 && group_size != 128)
     return fail(W4A8_ERR_INVALID, "group_size must be 64 or 128 (got %lld)", (long long)group_size);
   if (K <= 0 || K % group_size != 0)
@@ -132,7 +128,7 @@ int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_
                 (long long)N);
   if (M_total > INT32_MAX || E * N > INT32_MAX || K > INT32_MAX || E > 4096)
     return fail(W4A8_ERR_INVALID, "sizes exceed the 32-bit index range of the kernels");
-  if (M_total > 0 && (x_q == nullptr || x_scale == nullptr || out == nullptr))
+  if (M_total > 0 && (x_q == nullptr || x_scale == nullptr || (need_out && out == nullptr)))
     return fail(W4A8_ERR_INVALID, "null activation / output pointer");
   if (w_q4_packed == nullptr || w_scale == nullptr || w_zero == nullptr || expert_offsets == nullptr)
     return fail(W4A8_ERR_INVALID, "null weight / offset pointer");
@@ -140,33 +136,33 @@ int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_
   if (kernel != W4A8_KERNEL_AUTO && kernel != W4A8_KERNEL_TC && kernel != W4A8_KERNEL_SIMT &&
       kernel != W4A8_KERNEL_GEMV)
     return fail(W4A8_ERR_INVALID, "unknown kernel selector %d", kernel);
-  if (M_total == 0) return W4A8_OK;
+  a->x_q = x_q;
+  a->x_scale = x_scale;
+  a->w_packed = w_q4_packed;
+  a->w_scale = w_scale;
+  a->w_zero = w_zero;
+  a->offsets = expert_offsets;
+  a->out = static_cast<__nv_bfloat16*>(out);
+  a->x_stride0 = x_stride0;
+  a->M_total = static_cast<int>(M_total);
+  a->E = static_cast<int>(E);
+  a->N = static_cast<int>(N);
+  a->K = static_cast<int>(K);
+  a->gs = static_cast<int>(group_size);
+  return W4A8_OK;
+}
 
-  GemmArgs a{};
-  a.x_q = x_q;
-  a.x_scale = x_scale;
-  a.w_packed = w_q4_packed;
-  a.w_scale = w_scale;
-  a.w_zero = w_zero;
-  a.offsets = expert_offsets;
-  a.out = static_cast<__nv_bfloat16*>(out);
-  a.partials = partials;
+// Kernel choice and launch(es) of one grouped GEMM (the AUTO rule is
+// documented at W4A8_KERNEL_AUTO in the header).
+int gemm_dispatch(GemmArgs& a, int32_t kernel, void* stream) {
   a.status = device_status_ptr();
   if (a.status == nullptr) return fail(W4A8_ERR_CUDA, "cannot resolve the device status word");
-  a.x_stride0 = x_stride0;
-  a.out_stride0 = out_stride0;
-  a.out_stride1 = out_stride1;
-  a.M_total = static_cast<int>(M_total);
-  a.E = static_cast<int>(E);
-  a.N = static_cast<int>(N);
-  a.K = static_cast<int>(K);
-  a.gs = static_cast<int>(group_size);
-
-  const bool aligned16 = (reinterpret_cast<uintptr_t>(x_q) % 16 == 0) && (x_stride0 % 16 == 0) &&
-                         (reinterpret_cast<uintptr_t>(w_q4_packed) % 16 == 0);
-  const bool tc_ok = gemm_tc_supports((int)K, (int)group_size, (int)E) && aligned16;
+  const bool aligned16 = (reinterpret_cast<uintptr_t>(a.x_q) % 16 == 0) && (a.x_stride0 % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(a.w_packed) % 16 == 0);
+  const bool tc_ok = gemm_tc_supports(a.K, a.gs, a.E) && aligned16;
   const bool gemv_ok = aligned16;
-  const bool simt_ok = (reinterpret_cast<uintptr_t>(x_q) % 4 == 0) && (x_stride0 % 4 == 0);
+  const bool simt_ok = (reinterpret_cast<uintptr_t>(a.x_q) % 4 == 0) && (a.x_stride0 % 4 == 0);
+  const int64_t M_total = a.M_total, E = a.E;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaSuccess;
   switch (kernel) {
@@ -214,6 +210,53 @@ int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_
   }
   if (e != cudaSuccess) return cuda_fail(e, "grouped GEMM launch");
   return W4A8_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int w4a8_abi_version(void) { return 1; }
+
+const char* w4a8_last_error(void) { return g_last_error.c_str(); }
+
+int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
+                           const uint8_t* w_q4_packed, const float* w_scale, const int8_t* w_zero,
+                           const int32_t* expert_offsets, void* out, int64_t out_stride0,
+                           int64_t out_stride1, int64_t M_total, int64_t E, int64_t N, int64_t K,
+                           int64_t group_size, int32_t kernel, int32_t* partials, void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+  GemmArgs a{};
+  int rc = gemm_setup(&a, x_q, x_stride0, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, M_total, E, N, K,
+                      group_size, kernel, true, out);
+  if (rc != W4A8_OK || M_total == 0) return rc;
+  a.partials = partials;
+  a.out_stride0 = out_stride0;
+  a.out_stride1 = out_stride1;
+  return gemm_dispatch(a, kernel, stream);
+}
+
+int w4a8_group_gemm_moe_combine(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
+                                const uint8_t* w_q4_packed, const float* w_scale, const int8_t* w_zero,
+                                const int32_t* expert_offsets, const int32_t* sorted_ids, const float* topk_w,
+                                int64_t topk, float* acc_out, int64_t acc_stride0, int64_t M_total, int64_t E,
+                                int64_t N, int64_t K, int64_t group_size, int32_t kernel, void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+  GemmArgs a{};
+  int rc = gemm_setup(&a, x_q, x_stride0, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, M_total, E, N, K,
+                      group_size, kernel, false, nullptr);
+  if (rc != W4A8_OK) return rc;
+  if (topk <= 0 || topk > 256 || acc_stride0 < N)
+    return fail(W4A8_ERR_INVALID, "bad combine arguments topk=%lld acc_stride0=%lld (N=%lld)", (long long)topk,
+                (long long)acc_stride0, (long long)N);
+  if (M_total == 0) return W4A8_OK;
+  if (sorted_ids == nullptr || topk_w == nullptr || acc_out == nullptr)
+    return fail(W4A8_ERR_INVALID, "null combine pointer");
+  a.comb_out = acc_out;
+  a.comb_ids = sorted_ids;
+  a.comb_w = topk_w;
+  a.comb_topk = static_cast<int>(topk);
+  a.comb_stride = acc_stride0;
+  return gemm_dispatch(a, kernel, stream);
 }
 
 int w4a8_group_gemm_moe(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
@@ -304,6 +347,18 @@ int w4a8_moe_combine(const void* y, int64_t y_stride0, const int32_t* inv_pos, c
                                      (int)topk, (int)H, static_cast<__nv_bfloat16*>(out), out_stride0,
                                      static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? W4A8_OK : cuda_fail(e, "moe_combine launch");
+}
+
+int w4a8_combine_finish(float* acc, int64_t acc_stride0, int64_t T, int64_t H, void* out, int64_t out_stride0,
+                        void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+  if (T < 0 || H <= 0 || T > INT32_MAX || H > INT32_MAX || acc_stride0 < H || out_stride0 < H)
+    return fail(W4A8_ERR_INVALID, "bad sizes T=%lld H=%lld", (long long)T, (long long)H);
+  if (T == 0) return W4A8_OK;
+  if (acc == nullptr || out == nullptr) return fail(W4A8_ERR_INVALID, "null pointer");
+  cudaError_t e = launch_combine_finish(acc, acc_stride0, (int)T, (int)H, static_cast<__nv_bfloat16*>(out),
+                                        out_stride0, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? W4A8_OK : cuda_fail(e, "combine_finish launch");
 }
 
 int w4a8_gather_rows(const void* src, int64_t src_stride_bytes, const int32_t* index, int64_t rows,

@@ -35,6 +35,7 @@ enum DeviceStatus : int {
   kDevTimeoutTmemFull = 105,
   kDevTimeoutTmemEmpty = 106,
   kDevBadShape = 110,
+  kDevTimeoutSelfTest = 120,
 };
 
 // Roughly one second at B200 clocks.  A correct pipeline never waits this
@@ -84,21 +85,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait.  Returns false (after recording `code` in *status and raising
-// the CTA-local abort flag) when the wait expires or another role of the CTA
-// already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
-                                          volatile int* abort_flag) {
+// the CTA-local abort flag) when the wait has run `limit` cycles or another
+// role of the CTA already aborted.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int* status, int code,
+                                                volatile int* abort_flag, long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (*abort_flag) return false;
-    if (clock64() - t0 > W4A8_WAIT_LIMIT_CYCLES) {
+    if (clock64() - t0 > limit) {
       atomicCAS(status, 0, code);
       *abort_flag = 1;
       return false;
     }
   }
   return true;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
+                                          volatile int* abort_flag) {
+  return mbar_wait_limit(bar, parity, status, code, abort_flag, W4A8_WAIT_LIMIT_CYCLES);
 }
 
 // ----------------------------------------------------------------------------

@@ -188,6 +188,38 @@ moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int64_t y_stride0, const
   }
 }
 
+// Last step of the fused combine: out[t, :] = bf16(acc[t, :]) and acc[t, :]
+// = 0, so the accumulator is ready for the next batch without a memset.  One
+// CTA per (token, column slice); 16-byte vectors when the rows allow.
+__global__ void __launch_bounds__(kGThreads)
+combine_finish_kernel(float* __restrict__ acc, int64_t acc_stride0, int H, __nv_bfloat16* __restrict__ out,
+                      int64_t out_stride0) {
+  float* a = acc + static_cast<int64_t>(blockIdx.x) * acc_stride0;
+  __nv_bfloat16* o = out + static_cast<int64_t>(blockIdx.x) * out_stride0;
+  const bool vec = ((H & 7) == 0) && ((reinterpret_cast<uintptr_t>(a) & 15) == 0) &&
+                   ((reinterpret_cast<uintptr_t>(o) & 15) == 0);
+  if (vec) {
+    for (int c = blockIdx.y * kGThreads + threadIdx.x; c < H / 8; c += kGThreads * gridDim.y) {
+      float4* p = reinterpret_cast<float4*>(a) + 2 * c;
+      const float4 v0 = p[0], v1 = p[1];
+      p[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      p[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      uint4 r;
+      __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(&r);
+      r2[0] = __floats2bfloat162_rn(v0.x, v0.y);
+      r2[1] = __floats2bfloat162_rn(v0.z, v0.w);
+      r2[2] = __floats2bfloat162_rn(v1.x, v1.y);
+      r2[3] = __floats2bfloat162_rn(v1.z, v1.w);
+      reinterpret_cast<uint4*>(o)[c] = r;
+    }
+  } else {
+    for (int c = blockIdx.y * kGThreads + threadIdx.x; c < H; c += kGThreads * gridDim.y) {
+      o[c] = __float2bfloat16_rn(a[c]);
+      a[c] = 0.f;
+    }
+  }
+}
+
 // dst row i = src row index[i] (row_bytes bytes each); index < 0 leaves dst row i untouched.
 __global__ void __launch_bounds__(kGThreads)
 gather_rows_kernel(const uint8_t* __restrict__ src, int64_t src_stride, const int32_t* __restrict__ index,
@@ -246,6 +278,14 @@ cudaError_t launch_moe_combine(const __nv_bfloat16* y, int64_t y_stride0, const 
   const int slices = std::max(1, std::min(8, (H / 8 + kGThreads - 1) / kGThreads));   // column slices per token
   moe_combine_kernel<<<dim3(T, slices), kGThreads, 0, stream>>>(y, y_stride0, inv_pos, topk_w, topk, H, out,
                                                                  out_stride0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine_finish(float* acc, int64_t acc_stride0, int T, int H, __nv_bfloat16* out,
+                                  int64_t out_stride0, cudaStream_t stream) {
+  if (T <= 0) return cudaSuccess;
+  const int slices = std::max(1, std::min(8, (H / 8 + kGThreads - 1) / kGThreads));
+  combine_finish_kernel<<<dim3(T, slices), kGThreads, 0, stream>>>(acc, acc_stride0, H, out, out_stride0);
   return cudaGetLastError();
 }
 

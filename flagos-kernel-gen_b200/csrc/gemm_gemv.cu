@@ -255,11 +255,7 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const
     float v = acc[r];
 #pragma unroll
     for (int d = kSpan / 2; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
-    if (l == 0 && write) {
-      const int m = j.m0 + r;
-      a.out[static_cast<int64_t>(m) * a.out_stride0 + static_cast<int64_t>(j.n) * a.out_stride1] =
-          __float2bfloat16_rn(v * __ldg(a.x_scale + m));
-    }
+    if (l == 0 && write) store_output(a, j.m0 + r, j.n, v);
   }
 }
 

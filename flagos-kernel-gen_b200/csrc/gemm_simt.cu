@@ -99,12 +99,7 @@ gemm_simt_kernel(GemmArgs a) {
 #pragma unroll
       for (int i = 0; i < kSimtBM / 4; ++i) {
         const int r = tm + 4 * i;
-        if (r < tile.rows) {
-          const int m = tile.m0 + r;
-          const float y = acc[i] * a.x_scale[m];
-          a.out[static_cast<int64_t>(m) * a.out_stride0 + static_cast<int64_t>(n) * a.out_stride1] =
-              __float2bfloat16_rn(y);
-        }
+        if (r < tile.rows) store_output(a, tile.m0 + r, n, acc[i]);
       }
     }
   }

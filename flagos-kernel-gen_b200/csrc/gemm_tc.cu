@@ -557,11 +557,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
           const int col = wg * kEpiCols + 2 * c;
           if (col < tile.rows) {
             const int m = tile.m0 + col;
-            const float lo = __uint_as_float(static_cast<uint32_t>(acc[c]));
-            const float hi = __uint_as_float(static_cast<uint32_t>(acc[c] >> 32));
-            __nv_bfloat16* o = a.out + static_cast<int64_t>(m) * a.out_stride0 + static_cast<int64_t>(n) * a.out_stride1;
-            *o = __float2bfloat16_rn(lo * __ldg(a.x_scale + m));
-            if (col + 1 < tile.rows) o[a.out_stride0] = __float2bfloat16_rn(hi * __ldg(a.x_scale + m + 1));
+            store_output(a, m, n, __uint_as_float(static_cast<uint32_t>(acc[c])));
+            if (col + 1 < tile.rows) store_output(a, m + 1, n, __uint_as_float(static_cast<uint32_t>(acc[c] >> 32)));
           }
         }
       }

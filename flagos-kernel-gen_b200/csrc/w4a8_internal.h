@@ -26,7 +26,33 @@ struct GemmArgs {
   // other kernel of a split launch); default: every expert
   int min_rows = 1;
   int max_rows = 0x7fffffff;
+  // Fused top-k combine (comb_out != nullptr): instead of storing row m's
+  // bf16 result y to `out`, add topk_w[f] * y (fp32, y rounded to bf16 first,
+  // as the unfused combine reads it) into comb_out[f / comb_topk, n], where
+  // f = comb_ids[m] is the row's flat (token, slot) index.
+  float* comb_out = nullptr;
+  const int32_t* comb_ids = nullptr;
+  const float* comb_w = nullptr;
+  int comb_topk = 1;
+  int64_t comb_stride = 0;
 };
+
+#ifdef __CUDACC__
+// Output of row m, column n of a grouped GEMM: v is the fp32 group-scale sum,
+// the row's token scale is applied and the result rounded to bf16 (the
+// reference's store, docs/Task1.md:110-112); with the fused combine the
+// weighted bf16 value is added to the token's fp32 output row instead.
+__device__ __forceinline__ void store_output(const GemmArgs& a, int m, int n, float v) {
+  const __nv_bfloat16 y = __float2bfloat16_rn(v * __ldg(a.x_scale + m));
+  if (a.comb_out == nullptr) {
+    a.out[static_cast<int64_t>(m) * a.out_stride0 + static_cast<int64_t>(n) * a.out_stride1] = y;
+  } else {
+    const int f = __ldg(a.comb_ids + m);
+    const float w = __ldg(a.comb_w + f);
+    atomicAdd(a.comb_out + static_cast<int64_t>(f / a.comb_topk) * a.comb_stride + n, __fmul_rn(w, __bfloat162float(y)));
+  }
+}
+#endif
 
 cudaError_t launch_gemm_simt(const GemmArgs& a, cudaStream_t stream);
 cudaError_t launch_gemm_gemv(const GemmArgs& a, cudaStream_t stream);

@@ -65,7 +65,13 @@ class MoELayer:
     """Routed W4A8 MoE (gate/up -> SiLU-mul -> down, or a single up GEMM)."""
 
     def __init__(self, w13: W4A8Weights, w2: W4A8Weights | None, group_size: int, topk: int,
-                 max_tokens: int, align_block: int = 128):
+                 max_tokens: int, align_block: int = 128, fused_combine: bool = False):
+        """``fused_combine``: the last grouped GEMM adds its weighted rows into
+        an fp32 token accumulator in its epilogue (``w4a8_group_gemm_moe_combine``)
+        instead of writing [R, H] bf16 rows for a separate combine; the fp32
+        additions then run in no fixed order (results may differ from the
+        unfused, j-ascending combine in the last fp32 bit)."""
+        self.fused_combine = fused_combine
         self.w13, self.w2 = w13, w2
         self.gs, self.topk = group_size, topk
         E, N13, H = w13.shape
@@ -98,8 +104,13 @@ class MoELayer:
         if self.ffn:
             self.aq = torch.empty((R, I), dtype=torch.int8, device=dev)
             self.as_ = torch.empty((R,), dtype=torch.float32, device=dev)
-            self.y = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
-        self.out = torch.empty((max_tokens, H if self.ffn else I), dtype=torch.bfloat16, device=dev)
+            if not self.fused_combine:
+                self.y = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
+        width = H if self.ffn else I
+        self.out = torch.empty((max_tokens, width), dtype=torch.bfloat16, device=dev)
+        # fused combine: fp32 token accumulator, zero between batches (the
+        # finishing kernel clears the rows it converts)
+        self.acc = torch.zeros((max_tokens, width), dtype=torch.float32, device=dev) if self.fused_combine else None
 
     # number of library kernel launches per forward (for launch accounting)
     def launches_per_forward(self, tokens: int | None = None) -> int:
@@ -139,26 +150,40 @@ class MoELayer:
         ev.start("quant_scatter")
         ops.quant_scatter(x, self.inv_pos[:R], k, xq, xs)
         ev.stop()
+        if out is None:
+            out = self.out[:T]
+        fuse = self.fused_combine
+        tw = topk_weights if topk_weights.dtype == torch.float32 else topk_weights.float()
+        tw = tw.contiguous()
         h = self.h[:R]
         ev.start("gemm_gate_up")
-        ops.w4a8_group_gemm_moe(xq, xs, self.w13.packed, self.w13.scale, self.w13.zero, self.offsets, h, self.gs)
+        if fuse and not self.ffn:
+            ops.w4a8_group_gemm_moe_combine(xq, xs, self.w13.packed, self.w13.scale, self.w13.zero, self.offsets,
+                                            self.sorted_ids, tw, self.acc, self.gs)
+        else:
+            ops.w4a8_group_gemm_moe(xq, xs, self.w13.packed, self.w13.scale, self.w13.zero, self.offsets, h,
+                                    self.gs)
         ev.stop()
+        y = h
         if self.ffn:
             aq, as_ = self.aq[:R], self.as_[:R]
             ev.start("silu_mul_requant")
             ops.silu_mul_requant(h, aq, as_)
             ev.stop()
-            y = self.y[:R]
             ev.start("gemm_down")
-            ops.w4a8_group_gemm_moe(aq, as_, self.w2.packed, self.w2.scale, self.w2.zero, self.offsets, y,
-                                    self.gs)
+            if fuse:
+                ops.w4a8_group_gemm_moe_combine(aq, as_, self.w2.packed, self.w2.scale, self.w2.zero, self.offsets,
+                                                self.sorted_ids, tw, self.acc, self.gs)
+            else:
+                y = self.y[:R]
+                ops.w4a8_group_gemm_moe(aq, as_, self.w2.packed, self.w2.scale, self.w2.zero, self.offsets, y,
+                                        self.gs)
             ev.stop()
-        else:
-            y = h
-        if out is None:
-            out = self.out[:T]
         ev.start("combine")
-        out = ops.moe_combine(y, self.inv_pos[:R], topk_weights, out)
+        if fuse:
+            out = ops.combine_finish(self.acc, out)
+        else:
+            out = ops.moe_combine(y, self.inv_pos[:R], tw, out)
         ev.stop()
         return out
 

@@ -53,12 +53,12 @@ def _gemm_operands(x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, o
     assert K_half * 2 == K
     assert K % group_size == 0
     G = K // group_size
-    dev = _require_cuda(x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, out)
+    dev = _require_cuda(x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, *([] if out is None else [out]))
     if x_q.dtype != torch.int8:
         raise TypeError(f"x_q must be int8, got {x_q.dtype}")
-    if out.dtype != torch.bfloat16:
+    if out is not None and out.dtype != torch.bfloat16:
         raise TypeError(f"out must be bfloat16, got {out.dtype}")
-    if tuple(out.shape) != (M_total, N):
+    if out is not None and tuple(out.shape) != (M_total, N):
         raise ValueError(f"out must have shape {(M_total, N)}, got {tuple(out.shape)}")
     if tuple(w_scale.shape) != (E, N, G) or tuple(w_zero.shape) != (E, N, G):
         raise ValueError(f"w_scale / w_zero must have shape {(E, N, G)}")
@@ -128,6 +128,45 @@ def w4a8_group_gemm_moe_ex(x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_of
         w_scale.data_ptr(), w_zero.data_ptr(), expert_offsets.data_ptr(), out.data_ptr(), out.stride(0),
         out.stride(1), M_total, E, N, K, group_size, kernel, _ptr(partials), _stream(dev))
     _lib.check(rc, "w4a8_group_gemm_moe")
+    return out
+
+
+def w4a8_group_gemm_moe_combine(x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, sorted_ids,
+                                topk_weights, acc_out, group_size, kernel: int = _lib.KERNEL_AUTO):
+    """Grouped GEMM whose epilogue adds ``topk_weights[t, j] * y`` (y the bf16
+    row result of ``w4a8_group_gemm_moe``) into ``acc_out[t]`` (fp32 [T, N],
+    zero before the batch's first GEMM), t, j from ``sorted_ids`` (flat
+    t*topk + j per sorted row, as ``moe_align`` writes it).  Finish with
+    ``combine_finish``.  The fp32 additions run in no fixed order."""
+    dev, x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, M_total, E, N, K = _gemm_operands(
+        x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, None, group_size)
+    _require_cuda(x_q, sorted_ids, topk_weights, acc_out)
+    T, k = topk_weights.shape
+    tw = _contig(topk_weights, torch.float32, "topk_weights")
+    if sorted_ids.dtype != torch.int32 or sorted_ids.numel() < M_total:
+        raise ValueError("sorted_ids must be int32 with at least one entry per row")
+    if acc_out.dtype != torch.float32 or acc_out.dim() != 2 or acc_out.shape[1] != N or acc_out.shape[0] < T \
+            or acc_out.stride(1) != 1:
+        raise ValueError(f"acc_out must be fp32 [>= {T}, {N}] with unit column stride")
+    rc = _lib.load().w4a8_group_gemm_moe_combine(
+        x_q.data_ptr(), x_q.stride(0) if M_total > 0 else K, x_scale.data_ptr(), w_q4_packed.data_ptr(),
+        w_scale.data_ptr(), w_zero.data_ptr(), expert_offsets.data_ptr(), sorted_ids.data_ptr(), tw.data_ptr(), k,
+        acc_out.data_ptr(), acc_out.stride(0), M_total, E, N, K, group_size, kernel, _stream(dev))
+    _lib.check(rc, "w4a8_group_gemm_moe_combine")
+    return acc_out
+
+
+def combine_finish(acc: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out[t] = bf16(acc[t]) and acc[t] = 0 for t < out.shape[0]."""
+    dev = _require_cuda(acc, out)
+    T, H = out.shape
+    if acc.dtype != torch.float32 or acc.stride(1) != 1 or acc.shape[1] != H or acc.shape[0] < T:
+        raise ValueError("acc must be fp32 [>= T, H] with unit column stride")
+    if out.dtype != torch.bfloat16 or out.stride(1) != 1:
+        raise ValueError("out must be bf16 with unit column stride")
+    rc = _lib.load().w4a8_combine_finish(acc.data_ptr(), acc.stride(0), T, H, out.data_ptr(), out.stride(0),
+                                         _stream(dev))
+    _lib.check(rc, "combine_finish")
     return out
 
 

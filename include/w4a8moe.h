@@ -80,6 +80,34 @@ int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_
                            int64_t group_size, int32_t kernel, int32_t* partials, void* stream);
 
 /*
+ * Grouped W4A8 GEMM with the weighted top-k combine fused into its epilogue.
+ * Replaces the bf16 store of docs/Task1.md:110-112 (the reference's operator
+ * ends there) followed by a separate combine: each row m's result is still
+ * rounded to bf16 exactly as w4a8_group_gemm_moe stores it, then multiplied
+ * by its top-k weight in fp32 and added (fp32 atomics) into the token's row
+ *   acc_out[f / topk, n] += topk_w[f] * y[m, n],   f = sorted_ids[m]
+ * (f = t*topk + j, as written by w4a8_moe_align).  acc_out fp32 [T, N] (row
+ * stride acc_stride0) must hold zeros before the first GEMM of a batch;
+ * w4a8_combine_finish then writes the bf16 output and clears it again.  The
+ * order of the fp32 additions is not fixed, so results may differ from the
+ * unfused path (w4a8_moe_combine, j ascending) in the last fp32 bit.
+ * Other arguments as w4a8_group_gemm_moe_ex (no partials export).
+ */
+int w4a8_group_gemm_moe_combine(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
+                                const uint8_t* w_q4_packed, const float* w_scale, const int8_t* w_zero,
+                                const int32_t* expert_offsets, const int32_t* sorted_ids, const float* topk_w,
+                                int64_t topk, float* acc_out, int64_t acc_stride0, int64_t M_total, int64_t E,
+                                int64_t N, int64_t K, int64_t group_size, int32_t kernel, void* stream);
+
+/*
+ * Finishes a fused combine (no reference counterpart):
+ *   out[t, :] = bf16(acc[t, :]);  acc[t, :] = 0      for t < T
+ *   acc fp32 [T, H] (row stride acc_stride0), out bf16 [T, H] (row stride out_stride0)
+ */
+int w4a8_combine_finish(float* acc, int64_t acc_stride0, int64_t T, int64_t H, void* out,
+                        int64_t out_stride0, void* stream);
+
+/*
  * Per-token symmetric int8 quantisation of bf16 activations.
  * No counterpart kernel in the reference (its entry point takes x_q/x_scale
  * already quantised, docs/Task1.md:9-10); the convention is the repository's
@@ -170,6 +198,21 @@ int w4a8_moe_align_noalloc(const int32_t* topk_ids, int64_t T, int64_t topk, int
                            int64_t block_size, int32_t* expert_offsets, int32_t* sorted_ids,
                            int32_t* inv_pos, int32_t* padded_ids, int32_t* block_expert,
                            int32_t* num_post_pad, void* stream);
+
+/*
+ * Health check of the failure-detection path (no reference counterpart; the
+ * reference kernels have no bounded waits).  Launches one small kernel in
+ * which a thread waits on an mbarrier that is never completed, with a limit
+ * of limit_cycles (0 < limit_cycles <= the production limit of ~2e9
+ * cycles), while a second warp waits on another such barrier with the
+ * production limit.  The first wait runs out and records status code 120 in
+ * the device status word; the second leaves through the kernel's abort flag;
+ * the kernel returns.  No TMA, MMA or other asynchronous work is issued.
+ * report: int32 [3] device memory: [0] = first wait succeeded (expect 0),
+ * [1] = second wait succeeded (expect 0), [2] = kilocycles the second waited.
+ * Read the status with w4a8_device_status afterwards.
+ */
+int w4a8_selftest_wait_timeout(int64_t limit_cycles, int32_t* report, void* stream);
 
 /*
  * Reads (and, if reset != 0, clears) the device status word that the kernels

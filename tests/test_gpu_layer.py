@@ -192,3 +192,56 @@ def test_host_pipeline_matches_direct_forward(pkg, cuda):
     torch.cuda.synchronize()
     for d, o in zip(direct, outs):
         assert torch.equal(d.cpu(), o)
+
+
+@pytest.mark.parametrize("kernel", ["AUTO", "TC", "GEMV", "SIMT"])
+def test_fused_combine_gemm_each_kernel(pkg, cuda, kernel):
+    """w4a8_group_gemm_moe_combine: each kernel's epilogue adds topk_w * bf16(y)
+    into the token rows.  Against the unfused GEMM followed by the j-ascending
+    combine it may differ only by the order of the fp32 additions: every
+    element within the layer rule, and nearly all bit-identical."""
+    W = pkg.workloads
+    c = W.MoEConfig("t", hidden=1024, inter=768, experts=16, topk=4, zipf=1.2)
+    T = 200
+    inp = W.make_moe_inputs(c, T, seed=12, zero_mode="random")
+    al = pkg.moe_align(inp.topk_ids.to(cuda), c.experts)
+    xq, xs = pkg.quant_scatter(inp.x.to(cuda), al.inv_pos, c.topk)
+    w = [t.to(cuda) for t in inp.w2]             # down projection: [E, 1024, 768]
+    aq = xq[:, :768].contiguous()
+    sel = getattr(pkg, f"KERNEL_{kernel}")
+    R = T * c.topk
+    y = torch.empty((R, c.hidden), dtype=torch.bfloat16, device=cuda)
+    pkg.w4a8_group_gemm_moe_ex(aq, xs, *w, al.expert_offsets, y, c.group_size, kernel=sel)
+    tw = inp.topk_weights.to(cuda)
+    ref = pkg.moe_combine(y, al.inv_pos, tw)
+    acc = torch.zeros((T, c.hidden), dtype=torch.float32, device=cuda)
+    pkg.w4a8_group_gemm_moe_combine(aq, xs, *w, al.expert_offsets, al.sorted_ids, tw, acc, c.group_size,
+                                    kernel=sel)
+    out = torch.empty((T, c.hidden), dtype=torch.bfloat16, device=cuda)
+    pkg.combine_finish(acc, out)
+    torch.cuda.synchronize()
+    assert pkg.device_status() == 0
+    assert int(torch.count_nonzero(acc)) == 0, "combine_finish must clear the accumulator"
+    assert_layer_close(out, ref, c.hidden, f"fused combine ({kernel})")
+    same = (out.view(torch.int16) == ref.view(torch.int16)).float().mean().item()
+    assert same >= 0.99, same
+
+
+@pytest.mark.parametrize("cfg_name,T", [("_ffn", 96), ("small", 64)])
+def test_layer_fused_combine_against_oracle(pkg, cuda, cfg_name, T):
+    """MoELayer(fused_combine=True) against the oracle layer, twice in a row
+    (the accumulator must come back cleared), FFN and single-GEMM forms."""
+    W = pkg.workloads
+    c = W.MoEConfig("_ffn", hidden=512, inter=256, experts=16, topk=4, zipf=1.2) if cfg_name == "_ffn" \
+        else W.CONFIGS[cfg_name]
+    inp = W.make_moe_inputs(c, T, seed=3, zero_mode="random")
+    w13 = pkg.W4A8Weights(*[t.to(cuda) for t in inp.w13])
+    w2 = pkg.W4A8Weights(*[t.to(cuda) for t in inp.w2]) if inp.w2 is not None else None
+    layer = pkg.MoELayer(w13, w2, c.group_size, c.topk, T, fused_combine=True)
+    outs = [layer(inp.x.to(cuda), inp.topk_ids.to(cuda), inp.topk_weights.to(cuda)).clone() for _ in range(2)]
+    torch.cuda.synchronize()
+    assert pkg.device_status() == 0
+    ref = O.moe_layer(inp.x, inp.topk_ids, inp.topk_weights, inp.w13, inp.w2, c.group_size)
+    width = c.hidden if inp.w2 is not None else c.inter
+    for o in outs:
+        assert_layer_close(o, ref, width, "fused layer")
