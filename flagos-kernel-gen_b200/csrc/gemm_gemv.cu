@@ -187,7 +187,7 @@ __device__ __forceinline__ void partials_wrap(const uint8_t* wg, const uint8_t* 
 // finishes the output.  NG groups of a lane are in flight at once.  HALF:
 // rows with at most 16 K-groups are taken two per warp, one per half-warp
 // (`write` is false for a half-warp without a row of its own).
-template <int R, int GS, int NG, bool HALF>
+template <int R, int GS, int NG, bool HALF, bool kCombine>
 __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const TokenTile& tt, int G, int lane,
                                        bool write) {
   constexpr int kRot = GS == 128 ? 1 : 2;       // lane -> chunk rotation (conflict-free quarter warps)
@@ -246,7 +246,7 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const
       for (int r = 0; r < R; ++r) {
         acc[r] = fmaf(static_cast<float>(p[n][r]), ws, acc[r]);
         if (a.partials != nullptr && write)
-          a.partials[(static_cast<int64_t>(j.m0 + r) * a.N + j.n) * G + g[n]] = p[n][r];
+          a.partials[(static_cast<int64_t>(g[n]) * a.M_total + j.m0 + r) * a.N + j.n] = p[n][r];
       }
     }
   }
@@ -255,7 +255,15 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const
     float v = acc[r];
 #pragma unroll
     for (int d = kSpan / 2; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
-    if (l == 0 && write) store_output(a, j.m0 + r, j.n, v);
+    if (l == 0 && write) {
+      const int m = j.m0 + r;
+      if constexpr (kCombine) {
+        store_output(a, m, j.n, v);   // fused top-k combine into the token's fp32 row
+      } else {
+        a.out[static_cast<int64_t>(m) * a.out_stride0 + static_cast<int64_t>(j.n) * a.out_stride1] =
+            __float2bfloat16_rn(v * __ldg(a.x_scale + m));
+      }
+    }
   }
 }
 
@@ -358,8 +366,9 @@ __device__ __noinline__ void cost_balanced_range(int E, int NB, const int* cnt, 
 
 // kShort: every row has at most 16 K-groups and a warp takes two rows, one
 // per half-warp (a separate instantiation, so neither mode's register
-// allocation pays for the other's code).
-template <bool kShort>
+// allocation pays for the other's code).  kCombine: the fused top-k combine
+// store (also its own instantiation).
+template <bool kShort, bool kCombine>
 __global__ void __launch_bounds__(kGvThreads, 2)
 gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
   extern __shared__ unsigned char smem_raw[];
@@ -464,17 +473,17 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
                            static_cast<int64_t>(tile.e) * a.N + n0 + ri};
           if (a.gs == 128) {
             switch (tile.rows) {   // warp-uniform: the tile's token count
-              case 1: gv_row<1, 128, 1, true>(a, job, tt, G, lane, write); break;
-              case 2: gv_row<2, 128, 1, true>(a, job, tt, G, lane, write); break;
-              case 3: gv_row<3, 128, 1, true>(a, job, tt, G, lane, write); break;
-              default: gv_row<4, 128, 1, true>(a, job, tt, G, lane, write); break;
+              case 1: gv_row<1, 128, 1, true, kCombine>(a, job, tt, G, lane, write); break;
+              case 2: gv_row<2, 128, 1, true, kCombine>(a, job, tt, G, lane, write); break;
+              case 3: gv_row<3, 128, 1, true, kCombine>(a, job, tt, G, lane, write); break;
+              default: gv_row<4, 128, 1, true, kCombine>(a, job, tt, G, lane, write); break;
             }
           } else {
             switch (tile.rows) {
-              case 1: gv_row<1, 64, 1, true>(a, job, tt, G, lane, write); break;
-              case 2: gv_row<2, 64, 1, true>(a, job, tt, G, lane, write); break;
-              case 3: gv_row<3, 64, 1, true>(a, job, tt, G, lane, write); break;
-              default: gv_row<4, 64, 1, true>(a, job, tt, G, lane, write); break;
+              case 1: gv_row<1, 64, 1, true, kCombine>(a, job, tt, G, lane, write); break;
+              case 2: gv_row<2, 64, 1, true, kCombine>(a, job, tt, G, lane, write); break;
+              case 3: gv_row<3, 64, 1, true, kCombine>(a, job, tt, G, lane, write); break;
+              default: gv_row<4, 64, 1, true, kCombine>(a, job, tt, G, lane, write); break;
             }
           }
         }
@@ -485,17 +494,17 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
                            static_cast<int64_t>(tile.e) * a.N + n0 + rr};
           if (a.gs == 128) {
             switch (tile.rows) {   // warp-uniform: the tile's token count
-              case 1: gv_row<1, 128, 2, false>(a, job, tt, G, lane, true); break;
-              case 2: gv_row<2, 128, 2, false>(a, job, tt, G, lane, true); break;
-              case 3: gv_row<3, 128, 1, false>(a, job, tt, G, lane, true); break;
-              default: gv_row<4, 128, 1, false>(a, job, tt, G, lane, true); break;
+              case 1: gv_row<1, 128, 2, false, kCombine>(a, job, tt, G, lane, true); break;
+              case 2: gv_row<2, 128, 2, false, kCombine>(a, job, tt, G, lane, true); break;
+              case 3: gv_row<3, 128, 1, false, kCombine>(a, job, tt, G, lane, true); break;
+              default: gv_row<4, 128, 1, false, kCombine>(a, job, tt, G, lane, true); break;
             }
           } else {
             switch (tile.rows) {
-              case 1: gv_row<1, 64, 2, false>(a, job, tt, G, lane, true); break;
-              case 2: gv_row<2, 64, 2, false>(a, job, tt, G, lane, true); break;
-              case 3: gv_row<3, 64, 1, false>(a, job, tt, G, lane, true); break;
-              default: gv_row<4, 64, 1, false>(a, job, tt, G, lane, true); break;
+              case 1: gv_row<1, 64, 2, false, kCombine>(a, job, tt, G, lane, true); break;
+              case 2: gv_row<2, 64, 2, false, kCombine>(a, job, tt, G, lane, true); break;
+              case 3: gv_row<3, 64, 1, false, kCombine>(a, job, tt, G, lane, true); break;
+              default: gv_row<4, 64, 1, false, kCombine>(a, job, tt, G, lane, true); break;
             }
           }
         }
@@ -546,7 +555,8 @@ cudaError_t launch_gemm_gemv(const GemmArgs& a, cudaStream_t stream) {
   }
   const size_t smem = fixed + gp.stages * stage_bytes;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  auto kernel = G <= 16 ? gemm_gemv_kernel<true> : gemm_gemv_kernel<false>;
+  auto kernel = a.comb_out != nullptr ? (G <= 16 ? gemm_gemv_kernel<true, true> : gemm_gemv_kernel<false, true>)
+                                      : (G <= 16 ? gemm_gemv_kernel<true, false> : gemm_gemv_kernel<false, false>);
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 0;

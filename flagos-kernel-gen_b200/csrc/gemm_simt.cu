@@ -90,7 +90,7 @@ gemm_simt_kernel(GemmArgs a) {
           for (int c = 0; c < a.gs / 4; ++c) p = __dp4a(xrow[c], wrow[c], p);
           acc[i] = fmaf(static_cast<float>(p), ws, acc[i]);
           if (a.partials != nullptr && r < tile.rows) {
-            a.partials[(static_cast<int64_t>(tile.m0 + r) * a.N + n) * G + g] = p;
+            a.partials[(static_cast<int64_t>(g) * a.M_total + tile.m0 + r) * a.N + n] = p;
           }
         }
       }

@@ -44,10 +44,9 @@
 // depend on every loaded value have been stored, so no refill can overtake
 // an outstanding read.
 //
-// Register split (setmaxnreg): the producer/issuer warpgroup drops to 56,
-// the transform warpgroups to 56 (one) or 64 (two), the epilogue warpgroups
-// rise to 200: 128*(56 + 56 + 2*200) = 65536 or 128*(56 + 2*64 + 200) =
-// 49152, both within the launch's 512 x 128.
+// Register split (setmaxnreg), per tile configuration: the producer/issuer
+// and transform warpgroups drop, the epilogue warpgroups rise, within the
+// launch's 512 x 128 (see TcSmall / TcMid / TcWide).
 #include "common.cuh"
 #include "w4a8_internal.h"
 
@@ -57,6 +56,11 @@
 namespace w4a8 {
 
 namespace {
+// Epilogue variants of the kernel (separate instances, so the plain one
+// carries none of the others' code or registers):
+constexpr int kModePlain = 0;      // bf16 rows (the reference's store)
+constexpr int kModeCombine = 1;    // fused top-k combine into fp32 token rows
+constexpr int kModePartials = 2;   // int32 per-group partials only, no scale math, no bf16 store
 
 constexpr int kBW = 128;         // weight rows per tile (MMA M)
 constexpr int kBK = 128;         // K bytes per pipeline stage
@@ -71,10 +75,12 @@ constexpr uint32_t kMagicBits = 0x4B400000u;  // 1.5 * 2^23
 constexpr float kMagic = 12582912.0f;
 
 constexpr int kSeedBytes = 2048;   // two 1 KB swizzle atoms holding the accumulator-seed operands
+constexpr long long kDrainCycles = 20000000LL;   // ~10 ms: bounded drain after an aborted wait
 
 // Tile configurations.  kBT: token rows per tile (MMA N, rounded up to 16 per
-// tile at run time); kXStages / kAStages: depths of the token-tile and
-// unpacked-weight rings; kBufs: TMEM accumulators, alternating between the
+// tile at run time); kStages: depth of the token-tile and unpacked-weight
+// rings (one stage of each per K block, released together by one MMA commit
+// per group); kBufs: TMEM accumulators, alternating between the
 // two MMA issuers; kTransformWGs / kEpilogueWGs: warpgroups 1-3 split
 // between the int4 -> int8 transform (taking K blocks in turn) and the
 // epilogue (splitting the tile's columns).  With few tokens per tile the
@@ -82,11 +88,10 @@ constexpr int kSeedBytes = 2048;   // two 1 KB swizzle atoms holding the accumul
 // transform and by round trips through the rings, so narrower tiles trade
 // token-tile width for ring depth (and, at 64 tokens, a second transform
 // warpgroup).
-template <int BT, int XS, int AS, int NB, int TW, int EW, int TR, int ER, int XB>
+template <int BT, int S, int NB, int TW, int EW, int CR, int TR, int ER>
 struct TcConfig {
   static constexpr int kBT = BT;
-  static constexpr int kXStages = XS;
-  static constexpr int kAStages = AS;
+  static constexpr int kStages = S;
   static constexpr int kBufs = NB;
   static constexpr int kTransformWGs = TW;
   static constexpr int kEpilogueWGs = EW;
@@ -96,26 +101,30 @@ struct TcConfig {
   static constexpr int kEpiWarp0 = kTransformWarp0 + 4 * TW;
   static constexpr int kEpiWarps = 4 * kEpilogueWGs;
   static constexpr int kXBytes = BT * kBK;
-  // token rows per TMA box: a tile loads its rows rounded up to a box, so a
-  // large box over-fetches the next expert's rows at a tile's tail (for the
-  // 256-token tiles, 64-row boxes raised a launch's DRAM reads by a third)
-  static constexpr int kXBoxRows = XB;
+  // Token rows per TMA box: a tile loads its full 64-row boxes with one copy
+  // each and its ragged tail in 16-row boxes (so at most 15 rows of the next
+  // expert are over-fetched).  Copies of 2 KB could not keep the tensor core
+  // fed (measured on B200: 12 x 2 KB bulk copies per K-group took 2.1x the
+  // MMA time, 3 x 8 KB kept pace).
+  static constexpr int kXBoxRows = BT < 64 ? BT : 64;
+  static constexpr int kXTailRows = 16;
   static constexpr int kEpiCols = BT / kEpilogueWGs;   // columns per epilogue warpgroup
+  static constexpr int kControlRegs = CR;          // setmaxnreg of the producer / issuer warpgroup
   static constexpr int kTransformRegs = TR;        // setmaxnreg of the transform warpgroups
   static constexpr int kEpilogueRegs = ER;         // setmaxnreg of the epilogue warpgroups
   static constexpr size_t kSmemTiles =
-      size_t(kSeedBytes) + size_t(XS) * kXBytes + size_t(AS) * kABytes + size_t(kWStages) * kWBytes;
-  static constexpr int kNumBars = 2 * XS + 2 * kWStages + 2 * AS + 2 * NB;
+      size_t(kSeedBytes) + size_t(S) * kXBytes + size_t(S) * kABytes + size_t(kWStages) * kWBytes;
+  static constexpr int kNumBars = 3 * S + 2 * kWStages + 2 * NB + 2;   // + 2 abort-drain barriers
   static constexpr size_t smem_bytes(int E) {
     return 1024 /*alignment slack*/ + kSmemTiles + kNumBars * 8 + 16 + sizeof(int) * 3 * (E + 1);
   }
   static_assert(NB % 2 == 0 && NB * BT <= kTmemCols && TW >= 1 && TW <= 3 && EW >= 1 && kEpiCols % 32 == 0 &&
-                    BT % XB == 0 && XB % 8 == 0,
+                    BT % kXBoxRows == 0 && kXBoxRows % kXTailRows == 0 && S >= 2,
                 "tile configuration");
   // the register split must fit the launch's 512 x 128 registers, or a
   // setmaxnreg.inc waits forever
-  static_assert(128 * (56 + TW * TR + EW * ER) <= kThreads * (kLaunchRegs > 128 ? 128 : kLaunchRegs) &&
-                    TR % 8 == 0 && ER % 8 == 0,
+  static_assert(128 * (CR + TW * TR + EW * ER) <= kThreads * (kLaunchRegs > 128 ? 128 : kLaunchRegs) &&
+                    CR % 8 == 0 && TR % 8 == 0 && ER % 8 == 0,
                 "register split");
 };
 // Three tile widths, chosen per launch by the average rows per expert
@@ -123,9 +132,13 @@ struct TcConfig {
 // the 64-token tiles with a second transform warpgroup run 1.66 ms against
 // 2.18 ms for 256-token tiles; at 128 rows the 128-token tiles run 2.27 ms
 // against 3.41 ms; from ~200 rows on the 256-token tiles are fastest.
-using TcSmall = TcConfig<64, 6, 6, 8, 2, 1, 64, 200, 16>;    // up to 64 tokens per tile, two transform warpgroups
-using TcMid = TcConfig<128, 4, 4, 4, 1, 2, 56, 200, 32>;     // up to 128 tokens per tile
-using TcWide = TcConfig<256, 3, 2, 2, 1, 2, 56, 200, 16>;    // up to 256 tokens per tile
+using TcSmall = TcConfig<64, 6, 8, 2, 1, 56, 64, 200>;     // up to 64 tokens per tile, two transform warpgroups
+using TcMid = TcConfig<128, 4, 4, 1, 2, 56, 56, 200>;      // up to 128 tokens per tile
+// 256-token tiles: the int4 -> int8 transform of a weight block is paid once
+// per token tile, so the widest MMA (N = 256) gives it the fewest tiles
+// (192-token tiles with a double-buffered epilogue measured 31 % slower on
+// 256 experts x 512 rows).
+using TcWide = TcConfig<256, 3, 2, 1, 2, 56, 56, 200>;     // up to 256 tokens per tile
 constexpr int kSmallTileAvgRows = 48;    // average rows per expert up to which TcSmall runs
 constexpr int kMidTileAvgRows = 160;     // ... and TcMid
 static_assert(TcSmall::smem_bytes(kMaxExperts) <= 227 * 1024, "small configuration exceeds shared memory");
@@ -195,31 +208,31 @@ __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
   return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
 }
 
-template <class C>
+template <class C, int kMode>
 __global__ void __launch_bounds__(C::kThreads, 1)
-gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-               const GemmArgs a) {
-  constexpr int kBT = C::kBT, kXStages = C::kXStages, kAStages = C::kAStages, kBufs = C::kBufs;
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_xt,
+               const __grid_constant__ CUtensorMap tm_w, const GemmArgs a) {
+  constexpr int kBT = C::kBT, kStages = C::kStages, kBufs = C::kBufs;
   constexpr int kXBytes = C::kXBytes, kEpiCols = C::kEpiCols, kEpiWarp0 = C::kEpiWarp0;
-  constexpr int kXBoxRows = C::kXBoxRows;
+  constexpr int kXBoxRows = C::kXBoxRows, kXTailRows = C::kXTailRows;
   constexpr int kTransformWGs = C::kTransformWGs;
   extern __shared__ unsigned char smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sX = base;
-  uint8_t* sA = sX + kXStages * kXBytes;
-  uint8_t* sW = sA + kAStages * kABytes;
+  uint8_t* sA = sX + kStages * kXBytes;
+  uint8_t* sW = sA + kStages * kABytes;
   uint8_t* sSeed = sW + kWStages * kWBytes;   // [A atom | B atom], 1024-aligned
   uint64_t* bars = reinterpret_cast<uint64_t*>(sSeed + kSeedBytes);
   uint64_t* x_full = bars;
-  uint64_t* x_empty = x_full + kXStages;
-  uint64_t* w_full = x_empty + kXStages;
+  uint64_t* op_empty = x_full + kStages;   // token stage s and unpacked-weight stage s are free again
+  uint64_t* w_full = op_empty + kStages;
   uint64_t* w_empty = w_full + kWStages;
   uint64_t* a_full = w_empty + kWStages;
-  uint64_t* a_empty = a_full + kAStages;
-  uint64_t* tmem_full = a_empty + kAStages;
+  uint64_t* tmem_full = a_full + kStages;
   uint64_t* tmem_empty = tmem_full + kBufs;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + kBufs);
+  uint64_t* drain_bar = tmem_empty + kBufs;   // [2]: one per MMA issuer, used only after an abort
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* sched_mem = reinterpret_cast<int*>(tmem_slot + 4);
 
@@ -228,27 +241,27 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
 
   if (threadIdx.x == 0) {
     const int groups_per_block = kBK / a.gs;   // MMA issuers (one per group) that read a K block
-    for (int s = 0; s < kXStages; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&x_full[s], 1);
-      mbar_init(&x_empty[s], groups_per_block);   // one MMA commit per group of the block
+      mbar_init(&op_empty[s], groups_per_block);   // one MMA commit per group of the block
+      mbar_init(&a_full[s], 4);
     }
     for (int s = 0; s < kWStages; ++s) {
       mbar_init(&w_full[s], 1);
       mbar_init(&w_empty[s], 4);   // 4 transform warps
     }
-    for (int s = 0; s < kAStages; ++s) {
-      mbar_init(&a_full[s], 4);
-      mbar_init(&a_empty[s], groups_per_block);
-    }
     for (int b = 0; b < kBufs; ++b) {
       mbar_init(&tmem_full[b], 1);
       mbar_init(&tmem_empty[b], C::kEpiWarps);
     }
+    mbar_init(&drain_bar[0], 1);
+    mbar_init(&drain_bar[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_x);
+    prefetch_tmap(&tm_xt);
     prefetch_tmap(&tm_w);
   }
   if (warp == 1) {
@@ -279,7 +292,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   // Each warpgroup's branch starts with its own setmaxnreg, so the compiler
   // allocates the code that follows within that budget.
   if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::kControlRegs));
    // The producer and issuer warps run their loops with all 32 lanes (the
    // waits too), and only the TMA / MMA / commit instructions sit in a short
    // lane-0 block: a loop run by one lane of a diverged warp pays a
@@ -292,19 +305,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     uint32_t phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const Tile tile = sched_tile(sch, t);
-      const int nx = (tile.rows + kXBoxRows - 1) / kXBoxRows;
-      const uint32_t bytes = nx * kXBoxRows * kBK;
+      const int nbig = tile.rows / kXBoxRows;                                        // full boxes
+      const int ntail = (tile.rows - nbig * kXBoxRows + kXTailRows - 1) / kXTailRows;   // 16-row boxes
+      const uint32_t bytes = (nbig * kXBoxRows + ntail * kXTailRows) * kBK;
       for (int kb = 0; kb < KB; ++kb) {
-        if (!mbar_wait(&x_empty[stage], phase ^ 1, a.status, kDevTimeoutLoadEmpty, abort_flag))
+        if (!mbar_wait(&op_empty[stage], phase ^ 1, a.status, kDevTimeoutLoadEmpty, abort_flag))
           goto x_done;
         if (lane == 0) {
           mbar_arrive_expect_tx(&x_full[stage], bytes);
-          for (int j = 0; j < nx; ++j)
-            tma_load_2d(sX + stage * kXBytes + j * kXBoxRows * kBK, &tm_x, &x_full[stage], kb * kBK,
-                        tile.m0 + j * kXBoxRows, pol_x);
+          uint8_t* dst = sX + stage * kXBytes;
+          for (int j = 0; j < nbig; ++j)
+            tma_load_2d(dst + j * kXBoxRows * kBK, &tm_x, &x_full[stage], kb * kBK, tile.m0 + j * kXBoxRows, pol_x);
+          for (int j = 0; j < ntail; ++j)
+            tma_load_2d(dst + (nbig * kXBoxRows + j * kXTailRows) * kBK, &tm_xt, &x_full[stage], kb * kBK,
+                        tile.m0 + nbig * kXBoxRows + j * kXTailRows, pol_x);
         }
         __syncwarp();
-        if (++stage == kXStages) { stage = 0; phase ^= 1; }
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
     }
   x_done:;
@@ -348,8 +365,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
       constexpr uint64_t kSboMask = ~(static_cast<uint64_t>(0x3FFF) << 32);
       const uint64_t seed_a = make_desc_sw128(smem_u32(sSeed)) & kSboMask;          // row-group stride 0
       const uint64_t seed_b = make_desc_sw128(smem_u32(sSeed + 1024)) & kSboMask;
-      int stage = 0, astage = 0, c = 0;
-      uint32_t phase = 0, aphase = 0;
+      int stage = 0, c = 0;
+      uint32_t phase = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         const Tile tile = sched_tile(sch, t);
         const int n_mma = (tile.rows + 15) & ~15;
@@ -360,13 +377,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
           const bool block_end = (sub + 1 == gpk) || g == G - 1;
           if ((c & 1) == p) {
             if (!mbar_wait(&x_full[stage], phase, a.status, kDevTimeoutLoadFull, abort_flag)) goto mma_done;
-            if (!mbar_wait(&a_full[astage], aphase, a.status, kDevTimeoutAFull, abort_flag)) goto mma_done;
+            if (!mbar_wait(&a_full[stage], phase, a.status, kDevTimeoutAFull, abort_flag)) goto mma_done;
             const int buf = c % kBufs;
             const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kBT);
             if (!mbar_wait(&tmem_empty[buf], ((c / kBufs) & 1) ^ 1, a.status, kDevTimeoutTmemEmpty, abort_flag))
               goto mma_done;
             // descriptors advance by (byte offset >> 4) in their start-address field
-            const uint64_t adesc = desc_a0 + static_cast<uint64_t>((astage * kABytes + sub * kpg * 32) >> 4);
+            const uint64_t adesc = desc_a0 + static_cast<uint64_t>((stage * kABytes + sub * kpg * 32) >> 4);
             const uint64_t bdesc = desc_x0 + static_cast<uint64_t>((stage * kXBytes + sub * kpg * 32) >> 4);
             const bool trailing = block_end && sub + 1 < gpk;   // a trailing block with fewer groups than its count
             if (lane == 0) {
@@ -377,19 +394,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
               for (int ks = 0; ks < kpg; ++ks)
                 mma_i8_ss(d_tmem, adesc + 2 * ks, bdesc + 2 * ks, idesc, 1u);
               mma_commit(&tmem_full[buf]);
-              mma_commit(&x_empty[stage]);
-              mma_commit(&a_empty[astage]);
-              if (trailing) {
-                mma_commit(&x_empty[stage]);
-                mma_commit(&a_empty[astage]);
-              }
+              mma_commit(&op_empty[stage]);
+              if (trailing) mma_commit(&op_empty[stage]);
             }
             __syncwarp();
           }
           if (block_end) {
             sub = 0;
-            if (++stage == kXStages) { stage = 0; phase ^= 1; }
-            if (++astage == kAStages) { astage = 0; aphase ^= 1; }
+            if (++stage == kStages) { stage = 0; phase ^= 1; }
           } else {
             ++sub;
           }
@@ -427,7 +439,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         if constexpr (kTransformWGs > 1) {
           if (kb % kTransformWGs != tg) {   // the other warpgroup's block: advance the rings only
             if (++stage == kWStages) { stage = 0; phase ^= 1; }
-            if (++astage == kAStages) { astage = 0; aphase ^= 1; }
+            if (++astage == kStages) { astage = 0; aphase ^= 1; }
             continue;
           }
         }
@@ -461,7 +473,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         const int wstage = stage;
         if (++stage == kWStages) { stage = 0; phase ^= 1; }
 
-        if (!mbar_wait(&a_empty[astage], aphase ^ 1, a.status, kDevTimeoutAEmpty, abort_flag)) goto tr_done;
+        if (!mbar_wait(&op_empty[astage], aphase ^ 1, a.status, kDevTimeoutAEmpty, abort_flag)) goto tr_done;
         uint8_t* dst_row = sA + astage * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -489,7 +501,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
           mbar_arrive(&w_empty[wstage]);   // the stores above depend on every byte read from it
           mbar_arrive(&a_full[astage]);
         }
-        if (++astage == kAStages) { astage = 0; aphase ^= 1; }
+        if (++astage == kStages) { astage = 0; aphase ^= 1; }
       }
     }
   tr_done:;
@@ -500,6 +512,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     const int wg = (warp - kEpiWarp0) >> 2;           // column range of this warpgroup
     const int r = quarter * 32 + lane;                // weight row within the tile
     const uint64_t magic2 = f2_pack(kMagic, kMagic);
+    constexpr int kChunks = kEpiCols / 32;
     int buf = 0;
     uint32_t bphase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
@@ -509,6 +522,41 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
       const int n_mma = (tile.rows + 15) & ~15;
       const int my_cols = n_mma - wg * kEpiCols;      // columns of this warpgroup holding tokens (may be <= 0)
       const float* wsrow = a.w_scale + (static_cast<int64_t>(tile.e) * a.N + (valid ? n : 0)) * G;
+      if constexpr (kMode == kModePartials) {
+        // Partials export: each group's accumulator is drained and written as
+        // int32, [G, M_total, N] (consecutive lanes hold consecutive output
+        // channels, so every store is one 128-byte line).
+        for (int g = 0; g < G; ++g) {
+          if (!mbar_wait(&tmem_full[buf], bphase, a.status, kDevTimeoutTmemFull, abort_flag)) goto epi_done;
+          tc_fence_after();
+          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                 static_cast<uint32_t>(buf * kBT + wg * kEpiCols);
+#pragma unroll 1
+          for (int c32 = 0; c32 < kChunks; ++c32) {
+            const bool have = c32 * 32 < my_cols;   // warp-uniform
+            uint64_t d[16];
+            __syncwarp();
+            if (have) tmem_ld_x32_pairs(taddr + c32 * 32, d);
+            if (c32 == kChunks - 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&tmem_empty[buf]);
+            }
+            if (have && valid) {
+              int32_t* prow = a.partials + (static_cast<int64_t>(g) * a.M_total + tile.m0) * a.N + n;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const int col = wg * kEpiCols + c32 * 32 + j;
+                if (col < tile.rows)
+                  prow[static_cast<int64_t>(col) * a.N] =
+                      static_cast<int>(static_cast<uint32_t>(d[j >> 1] >> (32 * (j & 1))) - kMagicBits);
+              }
+            }
+          }
+          if (++buf == kBufs) { buf = 0; bphase ^= 1; }
+        }
+        continue;
+      }
       uint64_t acc[kEpiCols / 2];
 #pragma unroll
       for (int c = 0; c < kEpiCols / 2; ++c) acc[c] = 0;
@@ -522,14 +570,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                static_cast<uint32_t>(buf * kBT + wg * kEpiCols);
         // Drain 32 columns per load; the accumulator goes back to the MMA as
-        // soon as the last chunk is in registers, before its math.
+        // soon as the last chunk is in registers, before its math.  (Loading
+        // the next chunk while this one's math runs needs a second 32-column
+        // buffer, which does not fit the 256-token tile's registers.)
 #pragma unroll
-        for (int c32 = 0; c32 < kEpiCols / 32; ++c32) {
+        for (int c32 = 0; c32 < kChunks; ++c32) {
           const bool have = c32 * 32 < my_cols;   // warp-uniform
           uint64_t d[16];
           __syncwarp();
           if (have) tmem_ld_x32_pairs(taddr + c32 * 32, d);
-          if (c32 == kEpiCols / 32 - 1) {
+          if (c32 == kChunks - 1) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tmem_empty[buf]);
@@ -538,15 +588,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
 #pragma unroll
             for (int j = 0; j < 16; ++j)   // P + 1.5 * 2^23 read as fp32, minus 1.5 * 2^23 = float(P)
               acc[c32 * 16 + j] = f2_fma(f2_sub(d[j], magic2), ws2, acc[c32 * 16 + j]);
-            if (a.partials != nullptr && valid) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int col = wg * kEpiCols + c32 * 32 + j;
-                const uint32_t vj = static_cast<uint32_t>(d[j >> 1] >> (32 * (j & 1)));
-                if (col < tile.rows)
-                  a.partials[(static_cast<int64_t>(tile.m0 + col) * a.N + n) * G + g] = static_cast<int>(vj - kMagicBits);
-              }
-            }
           }
         }
         if (++buf == kBufs) { buf = 0; bphase ^= 1; }
@@ -557,8 +598,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
           const int col = wg * kEpiCols + 2 * c;
           if (col < tile.rows) {
             const int m = tile.m0 + col;
-            store_output(a, m, n, __uint_as_float(static_cast<uint32_t>(acc[c])));
-            if (col + 1 < tile.rows) store_output(a, m + 1, n, __uint_as_float(static_cast<uint32_t>(acc[c] >> 32)));
+            const float lo = __uint_as_float(static_cast<uint32_t>(acc[c]));
+            const float hi = __uint_as_float(static_cast<uint32_t>(acc[c] >> 32));
+            if constexpr (kMode == kModeCombine) {
+              // fused top-k combine: the weighted bf16 row result goes to its token's fp32 row
+              store_output(a, m, n, lo);
+              if (col + 1 < tile.rows) store_output(a, m + 1, n, hi);
+            } else {
+              __nv_bfloat16* o = a.out + static_cast<int64_t>(m) * a.out_stride0 + static_cast<int64_t>(n) * a.out_stride1;
+              *o = __float2bfloat16_rn(lo * __ldg(a.x_scale + m));
+              if (col + 1 < tile.rows) o[a.out_stride0] = __float2bfloat16_rn(hi * __ldg(a.x_scale + m + 1));
+            }
           }
         }
       }
@@ -566,6 +616,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   epi_done:;
   }
 
+  // A wait that gave up left the pipeline mid-flight: before TMEM is freed,
+  // each MMA issuer waits (bounded) for its own MMAs through one more commit,
+  // and every thread then idles a bounded while so TMA copies in flight land
+  // in shared memory before the CTA exits.
+  if (*abort_flag) {
+    if ((warp == 1 || warp == 3) && lane == 0) {
+      mma_commit(&drain_bar[warp == 1 ? 0 : 1]);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(&drain_bar[warp == 1 ? 0 : 1], 0) && clock64() - t0 < kDrainCycles) {
+      }
+    }
+    const long long t0 = clock64();
+    while (clock64() - t0 < kDrainCycles) {
+    }
+  }
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
@@ -602,19 +667,17 @@ bool encode_2d_u8(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t ou
   return r == CUDA_SUCCESS;
 }
 
-template <class C>
-cudaError_t launch_tc_config(const CUtensorMap& tm_w, const GemmArgs& a, cudaStream_t stream) {
-  CUtensorMap tm_x;
-  if (!encode_2d_u8(&tm_x, a.x_q, static_cast<uint64_t>(a.K), static_cast<uint64_t>(a.M_total),
-                    static_cast<uint64_t>(a.x_stride0), kBK, C::kXBoxRows, CU_TENSOR_MAP_SWIZZLE_128B))
-    return cudaErrorInvalidValue;
+template <class C, int kMode>
+cudaError_t launch_tc_kernel(const CUtensorMap& tm_x, const CUtensorMap& tm_xt, const CUtensorMap& tm_w,
+                             const GemmArgs& a, cudaStream_t stream) {
+  static_assert(kMode == kModePlain || kMode == kModeCombine || kMode == kModePartials, "epilogue mode");
   // The setmaxnreg split relies on the launch's 512 x 128 registers; with
   // fewer, the epilogue's setmaxnreg.inc could wait forever, so refuse to
   // launch.
   static int regs_checked = 0;
   if (!regs_checked) {
     cudaFuncAttributes fa;
-    cudaError_t e = cudaFuncGetAttributes(&fa, gemm_tc_kernel<C>);
+    cudaError_t e = cudaFuncGetAttributes(&fa, gemm_tc_kernel<C, kMode>);
     if (e != cudaSuccess) return e;
     if (fa.numRegs != C::kLaunchRegs) return cudaErrorInvalidConfiguration;
     regs_checked = 1;
@@ -623,11 +686,32 @@ cudaError_t launch_tc_config(const CUtensorMap& tm_w, const GemmArgs& a, cudaStr
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const size_t smem = C::smem_bytes(a.E);
-  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<C, kMode>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  gemm_tc_kernel<C><<<sms, C::kThreads, smem, stream>>>(tm_x, tm_w, a);
+  gemm_tc_kernel<C, kMode><<<sms, C::kThreads, smem, stream>>>(tm_x, tm_xt, tm_w, a);
   return cudaGetLastError();
+}
+
+template <class C>
+cudaError_t launch_tc_config(const CUtensorMap& tm_w, const GemmArgs& a, cudaStream_t stream) {
+  CUtensorMap tm_x, tm_xt;
+  if (!encode_2d_u8(&tm_x, a.x_q, static_cast<uint64_t>(a.K), static_cast<uint64_t>(a.M_total),
+                    static_cast<uint64_t>(a.x_stride0), kBK, C::kXBoxRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d_u8(&tm_xt, a.x_q, static_cast<uint64_t>(a.K), static_cast<uint64_t>(a.M_total),
+                    static_cast<uint64_t>(a.x_stride0), kBK, C::kXTailRows, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  // The fused combine and the int32 partials export are separate instances:
+  // the plain epilogue carries none of their code or registers (the
+  // combine's store path alone, compiled into the plain kernel, made it
+  // 1.4-1.9x slower).  With a partials export the plain kernel writes the
+  // bf16 rows and a second launch of the same pipeline writes the partials.
+  if (a.comb_out != nullptr) return launch_tc_kernel<C, kModeCombine>(tm_x, tm_xt, tm_w, a, stream);
+  GemmArgs plain = a;
+  plain.partials = nullptr;
+  cudaError_t e = launch_tc_kernel<C, kModePlain>(tm_x, tm_xt, tm_w, plain, stream);
+  if (e == cudaSuccess && a.partials != nullptr) e = launch_tc_kernel<C, kModePartials>(tm_x, tm_xt, tm_w, a, stream);
+  return e;
 }
 
 }  // namespace

@@ -18,7 +18,7 @@ struct GemmArgs {
   const int8_t* w_zero;       // [E, N, G] contiguous
   const int32_t* offsets;     // [E+1]
   __nv_bfloat16* out;         // [M_total, N] with strides (out_stride0, out_stride1) in elements
-  int32_t* partials;          // optional [M_total, N, G] int32 (debug / parity export)
+  int32_t* partials;          // optional [G, M_total, N] int32 (debug / parity export)
   int* status;                // device status word
   int64_t x_stride0, out_stride0, out_stride1;
   int M_total, E, N, K, gs;

@@ -115,19 +115,25 @@ def w4a8_group_gemm_moe(
 def w4a8_group_gemm_moe_ex(x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, out, group_size,
                            kernel: int = _lib.KERNEL_AUTO, partials: torch.Tensor | None = None):
     """``w4a8_group_gemm_moe`` with a kernel selector and the optional int32
-    per-group partial-sum export ``partials`` (int32 [M_total, N, K/group_size])."""
+    per-group partial-sum export ``partials`` (int32 [M_total, N, K/group_size],
+    the layout of the reference's einsum; the library writes it group-major,
+    [G, M_total, N], and it is transposed into ``partials`` here)."""
     dev, x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, M_total, E, N, K = _gemm_operands(
         x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, out, group_size)
+    staging = None
     if partials is not None:
         G = K // group_size
         if partials.dtype != torch.int32 or tuple(partials.shape) != (M_total, N, G) or not partials.is_contiguous():
             raise ValueError(f"partials must be a contiguous int32 tensor of shape {(M_total, N, G)}")
+        staging = torch.zeros((G, M_total, N), dtype=torch.int32, device=dev)
     lib = _lib.load()
     rc = lib.w4a8_group_gemm_moe_ex(
         x_q.data_ptr(), x_q.stride(0) if M_total > 0 else K, x_scale.data_ptr(), w_q4_packed.data_ptr(),
         w_scale.data_ptr(), w_zero.data_ptr(), expert_offsets.data_ptr(), out.data_ptr(), out.stride(0),
-        out.stride(1), M_total, E, N, K, group_size, kernel, _ptr(partials), _stream(dev))
+        out.stride(1), M_total, E, N, K, group_size, kernel, _ptr(staging), _stream(dev))
     _lib.check(rc, "w4a8_group_gemm_moe")
+    if staging is not None:
+        partials.copy_(staging.permute(1, 2, 0))
     return out
 
 

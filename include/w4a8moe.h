@@ -68,10 +68,11 @@ int w4a8_group_gemm_moe(const int8_t* x_q, int64_t x_stride0, const float* x_sca
 /*
  * Same as w4a8_group_gemm_moe with an explicit kernel choice and an optional
  * export of the exact int32 per-group partial sums
- *   partials[m, n, g] = sum_{k in group g} x_q[m,k] * int8(nibble - zero)
- * (int32 [M_total, N, K/group_size], written for rows inside a segment; NULL
- * to skip).  Replaces the per-group einsum of docs/Task1.md:100-104, which the
- * reference keeps internal.
+ *   partials[g, m, n] = sum_{k in group g} x_q[m,k] * int8(nibble - zero)
+ * (int32 [K/group_size, M_total, N], group-major so that the export is
+ * written in full lines; entries of rows inside a segment are written; NULL
+ * to skip).  Replaces the per-group einsum of docs/Task1.md:100-104, which
+ * the reference keeps internal (there as [m, n, g]).
  */
 int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
                            const uint8_t* w_q4_packed, const float* w_scale, const int8_t* w_zero,
