@@ -247,7 +247,7 @@ def cpu_full_step(cfg, T, seed=0):
 
 
 # ----------------------------------------------------------------------------- GPU leg
-def build_layer(pkg, cfg, T, rank, world, dev):
+def build_layer(pkg, cfg, T, rank, world, dev, transport="p2p"):
     W = pkg.workloads
     gen = W.make_generator(1000 + rank, dev)
     if world == 1:
@@ -257,7 +257,8 @@ def build_layer(pkg, cfg, T, rank, world, dev):
             if cfg.ffn else None
         return pkg.MoELayer(w13, w2, cfg.group_size, cfg.topk, T)
     ep = importlib.import_module(PKG_NAME + ".ep")
-    return ep.ExpertParallelMoE.with_synthetic_weights(cfg, T, rank, world, dev, gen)
+    cls = ep.P2PExpertParallelMoE if transport == "p2p" else ep.ExpertParallelMoE
+    return cls.with_synthetic_weights(cfg, T, rank, world, dev, gen)
 
 
 def kernel_bench(pkg, spec: str, steps: int, warmup: int, kernel: int):
@@ -499,6 +500,8 @@ def main():
                     help="skip the parity check, the target points and the routing variant")
     ap.add_argument("--cpu-budget", type=float, default=6.0, help="seconds of CPU work per baseline step")
     ap.add_argument("--kernel", type=int, default=0, help="kernel-only mode: 0 auto, 1 tensor core, 2 CUDA core")
+    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
+                    help="expert-parallel transport for N > 1: peer-memory kernels (default) or NCCL all-to-all")
     args = ap.parse_args()
     if args.workload.startswith("gemm_"):
         kernel_bench(importlib.import_module(PKG_NAME), args.workload, args.steps, args.warmup, args.kernel)
@@ -511,7 +514,7 @@ def main():
     config = {"workload": args.workload, "tokens_per_gpu": T, "hidden": cfg.hidden, "moe_inter": cfg.inter,
               "experts": cfg.experts, "topk": cfg.topk, "group_size": cfg.group_size,
               "routing": f"{cfg.scoring}" + (f"+zipf{cfg.zipf}" if cfg.zipf else " uniform"),
-              "parallelism": f"ep{world}" if world > 1 else "single", "l2": "inputs larger than L2 "
+              "parallelism": f"ep{world} ({args.ep_transport})" if world > 1 else "single", "l2": "inputs larger than L2 "
               "(expert weights are GBs; no flush needed)"}
 
     if args.impl == "reference":
@@ -551,7 +554,7 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     W = pkg.workloads
-    layer = build_layer(pkg, cfg, T, rank, world, dev)
+    layer = build_layer(pkg, cfg, T, rank, world, dev, args.ep_transport)
     inp = W.make_moe_inputs(cfg, T, seed=7 + rank, device=dev, weights=False)
     x, ids, tw = inp.x, inp.topk_ids, inp.topk_weights
 

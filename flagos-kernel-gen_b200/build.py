@@ -29,6 +29,7 @@ SOURCES = [
     "gemm_gemv.cu",
     "noalloc.cu",
     "health.cu",
+    "ep_p2p.cu",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -9,6 +9,7 @@
 // against any IEEE restatement of the same formula.
 #include "common.cuh"
 #include "w4a8_internal.h"
+#include "ep_p2p.cuh"
 
 namespace w4a8 {
 
@@ -40,14 +41,36 @@ __device__ __forceinline__ int8_t quant1(float x, float s) {
   return static_cast<int8_t>(__float2int_rz(q));
 }
 
-// One CTA per token row.  rows_out: nullptr -> write row t to out row t;
-// otherwise write row t to rows_out[t*topk + j] for j in [0, topk).  On the
-// vector path each element is quantised once, into registers, and the packed
-// row is then stored to every destination.
+}  // namespace
+
+// Destinations of a quantised token row: row t of one local array, or (with
+// rows_out) rows rows_out[t*topk + j] of it, j < topk.
+struct LocalRows {
+  int8_t* q;
+  int64_t q_stride0;
+  float* s;
+  const int32_t* rows_out;
+  int topk;
+  __device__ __forceinline__ int count() const { return rows_out ? topk : 1; }
+  // row pointer of destination d (nullptr: none); the thread with
+  // threadIdx.x == d also stores the scale
+  __device__ __forceinline__ int8_t* row(int t, int d, float scale, bool meta) const {
+    const int64_t r = rows_out ? rows_out[static_cast<int64_t>(t) * topk + d] : t;
+    if (r < 0) return nullptr;   // slot routed to no local expert
+    if (meta) s[r] = scale;
+    return q + r * q_stride0;
+  }
+};
+
+namespace {
+
+// One CTA per token row.  On the vector path each element is quantised once,
+// into registers, and the packed row is then stored to every destination
+// (Dest: LocalRows here, the peer receive buffers of ep_p2p.cu for the
+// expert-parallel dispatch).
+template <class Dest>
 __global__ void __launch_bounds__(kQThreads)
-act_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride0, int H,
-                 int8_t* __restrict__ q_out, int64_t q_stride0, float* __restrict__ s_out,
-                 const int32_t* __restrict__ rows_out, int topk) {
+act_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride0, int H, const Dest dest) {
   __shared__ float red[32];
   const int t = blockIdx.x;
   const __nv_bfloat16* xr = x + static_cast<int64_t>(t) * x_stride0;
@@ -75,11 +98,8 @@ act_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride0, int H,
   }
   amax = block_max(amax, red);
   const float s = fmaxf(__fdiv_rn(amax, 127.f), 1e-10f);
-  const int ndst = rows_out ? topk : 1;
-  if (threadIdx.x < ndst) {
-    const int64_t row = rows_out ? rows_out[static_cast<int64_t>(t) * topk + threadIdx.x] : t;
-    if (row >= 0) s_out[row] = s;
-  }
+  const int ndst = dest.count();
+  if (threadIdx.x < ndst) dest.row(t, threadIdx.x, s, true);   // scale and routing metadata
   // packed int8 row in registers (vector path): 8 values per uint2
   uint2 qv[kQMaxVec];
   if (vec) {
@@ -104,9 +124,8 @@ act_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride0, int H,
     }
   }
   for (int d = 0; d < ndst; ++d) {
-    const int64_t row = rows_out ? rows_out[static_cast<int64_t>(t) * topk + d] : t;
-    if (row < 0) continue;  // slot routed to no local expert
-    int8_t* qr = q_out + row * q_stride0;
+    int8_t* qr = dest.row(t, d, s, false);
+    if (qr == nullptr) continue;
     if (vec && ((reinterpret_cast<uintptr_t>(qr) & 7) == 0)) {
 #pragma unroll
       for (int i = 0; i < kQMaxVec; ++i) {
@@ -125,7 +144,14 @@ cudaError_t launch_act_quant(const __nv_bfloat16* x, int64_t x_stride0, int T, i
                              int64_t q_stride0, float* s, const int32_t* rows_out, int topk,
                              cudaStream_t stream) {
   if (T <= 0) return cudaSuccess;
-  act_quant_kernel<<<T, kQThreads, 0, stream>>>(x, x_stride0, H, q, q_stride0, s, rows_out, topk);
+  act_quant_kernel<LocalRows><<<T, kQThreads, 0, stream>>>(x, x_stride0, H, LocalRows{q, q_stride0, s, rows_out, topk});
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_dispatch(const __nv_bfloat16* x, int64_t x_stride0, int T, int H, const PeerRows& dest,
+                               cudaStream_t stream) {
+  if (T <= 0) return cudaSuccess;
+  act_quant_kernel<PeerRows><<<T, kQThreads, 0, stream>>>(x, x_stride0, H, dest);
   return cudaGetLastError();
 }
 

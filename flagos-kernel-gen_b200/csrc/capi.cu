@@ -162,7 +162,7 @@ int gemm_dispatch(GemmArgs& a, int32_t kernel, void* stream) {
   const bool tc_ok = gemm_tc_supports(a.K, a.gs, a.E) && aligned16;
   const bool gemv_ok = aligned16;
   const bool simt_ok = (reinterpret_cast<uintptr_t>(a.x_q) % 4 == 0) && (a.x_stride0 % 4 == 0);
-  const int64_t M_total = a.M_total, E = a.E;
+  const int64_t M_total = a.rows_hint > 0 ? a.rows_hint : a.M_total, E = a.E;   // rows the kernel choice assumes
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaSuccess;
   switch (kernel) {
@@ -233,6 +233,24 @@ int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_
   a.out_stride0 = out_stride0;
   a.out_stride1 = out_stride1;
   return gemm_dispatch(a, kernel, stream);
+}
+
+int w4a8_group_gemm_moe_hint(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
+                             const uint8_t* w_q4_packed, const float* w_scale, const int8_t* w_zero,
+                             const int32_t* expert_offsets, void* out, int64_t out_stride0, int64_t out_stride1,
+                             int64_t M_total, int64_t E, int64_t N, int64_t K, int64_t group_size,
+                             int64_t rows_hint, void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+  GemmArgs a{};
+  int rc = gemm_setup(&a, x_q, x_stride0, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, M_total, E, N, K,
+                      group_size, W4A8_KERNEL_AUTO, true, out);
+  if (rc != W4A8_OK || M_total == 0) return rc;
+  if (rows_hint < 0 || rows_hint > M_total)
+    return fail(W4A8_ERR_INVALID, "rows_hint %lld outside [0, M_total=%lld]", (long long)rows_hint, (long long)M_total);
+  a.out_stride0 = out_stride0;
+  a.out_stride1 = out_stride1;
+  a.rows_hint = static_cast<int>(rows_hint);
+  return gemm_dispatch(a, W4A8_KERNEL_AUTO, stream);
 }
 
 int w4a8_group_gemm_moe_combine(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
@@ -331,6 +349,19 @@ int w4a8_silu_mul_requant(const void* h, int64_t h_stride0, int64_t R, int64_t I
   if (h == nullptr || q == nullptr || s == nullptr) return fail(W4A8_ERR_INVALID, "null pointer");
   cudaError_t e = launch_silu_mul_requant(static_cast<const __nv_bfloat16*>(h), h_stride0, (int)R, (int)I, q, I,
                                           s, nullptr, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? W4A8_OK : cuda_fail(e, "silu_mul_requant launch");
+}
+
+int w4a8_silu_mul_requant_rows(const void* h, int64_t h_stride0, int64_t R, int64_t I, int8_t* q, float* s,
+                               const int32_t* valid_rows, void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+  if (R < 0 || I <= 0 || I > 16384 || R > INT32_MAX || h_stride0 < 2 * I)
+    return fail(W4A8_ERR_INVALID, "bad sizes R=%lld I=%lld (I <= 16384)", (long long)R, (long long)I);
+  if (R == 0) return W4A8_OK;
+  if (h == nullptr || q == nullptr || s == nullptr || valid_rows == nullptr)
+    return fail(W4A8_ERR_INVALID, "null pointer");
+  cudaError_t e = launch_silu_mul_requant(static_cast<const __nv_bfloat16*>(h), h_stride0, (int)R, (int)I, q, I,
+                                          s, valid_rows, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? W4A8_OK : cuda_fail(e, "silu_mul_requant launch");
 }
 

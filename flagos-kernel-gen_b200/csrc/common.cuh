@@ -36,6 +36,8 @@ enum DeviceStatus : int {
   kDevTimeoutTmemEmpty = 106,
   kDevBadShape = 110,
   kDevTimeoutSelfTest = 120,
+  kDevTimeoutPeer = 130,     // a peer rank's signal did not arrive (expert-parallel exchange / barrier)
+  kDevEpOverflow = 131,      // a rank would receive more rows than its receive buffer holds
 };
 
 // Roughly one second at B200 clocks.  A correct pipeline never waits this

@@ -60,8 +60,10 @@ silu_mul_requant_vec_kernel(const __nv_bfloat16* __restrict__ h, int64_t h_strid
                             int8_t* __restrict__ q, int64_t q_stride0, float* __restrict__ s_out,
                             const int32_t* __restrict__ valid_rows) {
   __shared__ float red[32];
-  const int64_t row = blockIdx.x;
-  if (valid_rows != nullptr && row >= *valid_rows) return;
+  // one row per CTA, or (valid_rows: a row count read on the device) a
+  // grid-stride loop over the rows below it
+  const int64_t lim = valid_rows != nullptr ? *valid_rows : gridDim.x;
+  for (int64_t row = blockIdx.x; row < lim; row += gridDim.x) {
   const __nv_bfloat16* hr = h + row * h_stride0;
   const int nv = I / 8;
   float y[kSVec][8];
@@ -95,6 +97,7 @@ silu_mul_requant_vec_kernel(const __nv_bfloat16* __restrict__ h, int64_t h_strid
       reinterpret_cast<uint2*>(qr)[v] = make_uint2(quant4(y[i][0], y[i][1], y[i][2], y[i][3], s),
                                                    quant4(y[i][4], y[i][5], y[i][6], y[i][7], s));
   }
+  }
 }
 
 // One CTA per row.  The fp32 products are staged in shared memory (I <= 16384).
@@ -104,8 +107,8 @@ silu_mul_requant_kernel(const __nv_bfloat16* __restrict__ h, int64_t h_stride0, 
                         const int32_t* __restrict__ valid_rows) {
   extern __shared__ float s_y[];
   __shared__ float red[32];
-  const int64_t row = blockIdx.x;
-  if (valid_rows != nullptr && row >= *valid_rows) return;
+  const int64_t lim = valid_rows != nullptr ? *valid_rows : gridDim.x;
+  for (int64_t row = blockIdx.x; row < lim; row += gridDim.x) {
   const __nv_bfloat16* hr = h + row * h_stride0;
   float amax = 0.f;
   const bool vec = ((I & 1) == 0) && ((reinterpret_cast<uintptr_t>(hr) & 3) == 0);
@@ -135,6 +138,8 @@ silu_mul_requant_kernel(const __nv_bfloat16* __restrict__ h, int64_t h_stride0, 
     float v = __fdiv_rn(s_y[i], s);
     v = fminf(fmaxf(v, -127.f), 127.f);
     qr[i] = static_cast<int8_t>(__float2int_rz(v));
+  }
+  __syncthreads();   // s_y is rewritten by the next row
   }
 }
 
@@ -254,6 +259,12 @@ cudaError_t launch_silu_mul_requant(const __nv_bfloat16* h, int64_t h_stride0, i
                                     int64_t q_stride0, float* s, const int32_t* valid_rows,
                                     cudaStream_t stream) {
   if (R <= 0) return cudaSuccess;
+  if (valid_rows != nullptr) {   // rows counted on the device: a resident grid strides over them
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    R = R < sms * 8 ? R : sms * 8;
+  }
   const bool vec = (I % 8) == 0 && I / 8 <= kGThreads * kSVec && (h_stride0 % 8) == 0 &&
                    (reinterpret_cast<uintptr_t>(h) % 16) == 0 && (q_stride0 % 8) == 0 &&
                    (reinterpret_cast<uintptr_t>(q) % 8) == 0;

@@ -731,7 +731,7 @@ cudaError_t launch_gemm_tc(const GemmArgs& a, cudaStream_t stream) {
 
   // Tile width by the average rows per expert (the launch's configuration is
   // fixed on the host, without a device synchronisation).
-  const int64_t rows = a.M_total, experts = a.E;
+  const int64_t rows = a.rows_hint > 0 ? a.rows_hint : a.M_total, experts = a.E;
   if (rows <= kSmallTileAvgRows * experts) return launch_tc_config<TcSmall>(tm_w, a, stream);
   if (rows <= kMidTileAvgRows * experts) return launch_tc_config<TcMid>(tm_w, a, stream);
   return launch_tc_config<TcWide>(tm_w, a, stream);

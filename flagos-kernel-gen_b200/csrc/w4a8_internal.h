@@ -26,6 +26,9 @@ struct GemmArgs {
   // other kernel of a split launch); default: every expert
   int min_rows = 1;
   int max_rows = 0x7fffffff;
+  // expected rows when M_total is only a capacity (the rows are counted on the
+  // device from the offsets): picks kernels and tile widths; 0 = M_total
+  int rows_hint = 0;
   // Fused top-k combine (comb_out != nullptr): instead of storing row m's
   // bf16 result y to `out`, add topk_w[f] * y (fp32, y rounded to bf16 first,
   // as the unfused combine reads it) into comb_out[f / comb_topk, n], where

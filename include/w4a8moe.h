@@ -81,6 +81,21 @@ int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_
                            int64_t group_size, int32_t kernel, int32_t* partials, void* stream);
 
 /*
+ * w4a8_group_gemm_moe (AUTO kernel choice) for a caller whose x_q / out hold
+ * M_total rows of capacity while the rows actually routed are known only on
+ * the device (expert_offsets[E] <= M_total, e.g. the receive buffer of the
+ * expert-parallel mode).  rows_hint (1..M_total, 0 = M_total) is the row
+ * count the kernel and tile-width choice assumes; results do not depend on
+ * it.  No reference counterpart (the reference reads the offsets on the
+ * host, Task1/v1.6/task1-codex5.5-all-v1.6.py:62-64).
+ */
+int w4a8_group_gemm_moe_hint(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
+                             const uint8_t* w_q4_packed, const float* w_scale, const int8_t* w_zero,
+                             const int32_t* expert_offsets, void* out, int64_t out_stride0,
+                             int64_t out_stride1, int64_t M_total, int64_t E, int64_t N, int64_t K,
+                             int64_t group_size, int64_t rows_hint, void* stream);
+
+/*
  * Grouped W4A8 GEMM with the weighted top-k combine fused into its epilogue.
  * Replaces the bf16 store of docs/Task1.md:110-112 (the reference's operator
  * ends there) followed by a separate combine: each row m's result is still
@@ -165,6 +180,14 @@ int w4a8_silu_mul_requant(const void* h, int64_t h_stride0, int64_t R, int64_t I
                           float* s, void* stream);
 
 /*
+ * w4a8_silu_mul_requant over the first *valid_rows rows (a count read on the
+ * device, at most R; R is the capacity of h / q / s).  No reference
+ * counterpart; used on the expert-parallel receive buffer.
+ */
+int w4a8_silu_mul_requant_rows(const void* h, int64_t h_stride0, int64_t R, int64_t I, int8_t* q,
+                               float* s, const int32_t* valid_rows, void* stream);
+
+/*
  * Weighted top-k combine back to token order (no reference counterpart):
  *   out[t, :] = bf16( sum_{j=0..topk-1} topk_w[t,j] * y[inv_pos[t*topk+j], :] )  (fp32, j ascending)
  *   y bf16 [*, H] (row stride y_stride0), topk_w fp32 [T, topk], out bf16 [T, H] (row stride out_stride0)
@@ -199,6 +222,47 @@ int w4a8_moe_align_noalloc(const int32_t* topk_ids, int64_t T, int64_t topk, int
                            int64_t block_size, int32_t* expert_offsets, int32_t* sorted_ids,
                            int32_t* inv_pos, int32_t* padded_ids, int32_t* block_expert,
                            int32_t* num_post_pad, void* stream);
+
+/*
+ * Expert parallelism over peer memory (no reference counterpart: the
+ * reference has no multi-GPU mode).  Every rank owns a receive buffer of one
+ * layout, mapped into every peer (peers: device array [world] of the buffers'
+ * base addresses as seen from this GPU, e.g. torch symmetric memory).  Byte
+ * offsets (identical on all ranks): flags int32 [world] (zero before the
+ * first epoch), counts int32 [world, E], xq int8 [cap_rows, H], xs fp32
+ * [cap_rows], src int32 [cap_rows], yhome bf16 [tk_max, H]; tk_max = the
+ * most slots (tokens x topk) one rank routes.  All ranks make the same calls
+ * in the same order with increasing epochs.  Waits on peers are bounded
+ * (~2 s): on expiry the kernel records code 130 in the device status word
+ * and returns; a rank that would receive more than cap_rows rows records 131
+ * and nothing is sent to it.
+ *
+ * w4a8_ep_exchange: this rank's rows per global expert (from its
+ *   w4a8_moe_align expert_offsets [E+1]) into every peer's counts row
+ *   `rank`, one signal of `epoch`, then dest_base int32 [E] (first receive
+ *   row of this rank's slots of expert e on its owner, -1 if none) and
+ *   local_offsets int32 [E/world + 1] (segments of this rank's experts in its
+ *   own xq; local_offsets[E/world] = rows received).
+ * w4a8_ep_dispatch: quantises each token once (as w4a8_act_quant) and stores
+ *   its row, scale and return address into the owners' receive buffers;
+ *   home_pos int32 [T*topk] = the slot's index, or -1 for dropped slots.
+ * w4a8_ep_barrier: every rank signals `epoch` and waits for all.
+ * w4a8_ep_return: row r of y (this rank's receive order, r < *total_rows)
+ *   into row f of its sender's yhome (src[r] = sender * tk_max + f).
+ */
+int w4a8_ep_exchange(const int32_t* expert_offsets, int64_t E, int64_t world, int64_t rank,
+                     void* const* peers, int64_t counts_off, int64_t flags_off, int32_t epoch,
+                     int64_t cap_rows, int32_t* dest_base, int32_t* local_offsets, void* stream);
+int w4a8_ep_dispatch(const void* x, int64_t x_stride0, int64_t T, int64_t H, const int32_t* topk_ids,
+                     int64_t topk, int64_t E, int64_t world, int64_t rank, int64_t tk_max,
+                     const int32_t* expert_offsets, const int32_t* inv_pos, const int32_t* dest_base,
+                     void* const* peers, int64_t xq_off, int64_t xs_off, int64_t src_off,
+                     int32_t* home_pos, void* stream);
+int w4a8_ep_barrier(void* const* peers, int64_t flags_off, int64_t world, int64_t rank, int32_t epoch,
+                    void* stream);
+int w4a8_ep_return(const void* y, int64_t y_stride0, int64_t H, const int32_t* src,
+                   const int32_t* total_rows, int64_t rows_hint, int64_t tk_max, void* const* peers,
+                   int64_t yhome_off, void* stream);
 
 /*
  * Health check of the failure-detection path (no reference counterpart; the

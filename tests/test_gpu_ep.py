@@ -1,6 +1,7 @@
-"""Expert parallelism over NCCL on 2 GPUs (skipped with fewer): every rank's
-output of ep.ExpertParallelMoE equals, bit for bit, a single-GPU MoELayer run
-over the tokens of all ranks (same weights).  Rows reach an expert in a
+"""Expert parallelism on 2 GPUs (skipped with fewer), both transports (the
+peer-memory kernels and NCCL all-to-all): every rank's output equals, bit for
+bit, a single-GPU MoELayer run over the tokens of all ranks (same weights),
+and a second forward through the same buffers gives the same bits.  Rows reach an expert in a
 different order under EP, but each row's result does not depend on the other
 rows of its segment, and the combine sums in the same slot order."""
 import datetime
@@ -26,7 +27,7 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, q, zipf):
+def _worker(rank, world, port, q, zipf, transport):
     try:
         sys.path.insert(0, REPO)
         import torch.distributed as dist
@@ -47,8 +48,14 @@ def _worker(rank, world, port, q, zipf):
         T = 96 + 32 * rank
         toks = [W.make_moe_inputs(cfg, 96 + 32 * r, seed=300 + r, weights=False) for r in range(world)]
         mine = toks[rank]
-        layer = ep.ExpertParallelMoE(w13, w2, cfg.experts, cfg.group_size, cfg.topk)
+        if transport == "p2p":
+            layer = ep.P2PExpertParallelMoE(w13, w2, cfg.experts, cfg.group_size, cfg.topk, max_tokens=256)
+        else:
+            layer = ep.ExpertParallelMoE(w13, w2, cfg.experts, cfg.group_size, cfg.topk)
         out = layer(mine.x.to(dev), mine.topk_ids.to(dev), mine.topk_weights.to(dev)).clone()
+        out2 = layer(mine.x.to(dev), mine.topk_ids.to(dev), mine.topk_weights.to(dev)).clone()   # buffers reused
+        torch.cuda.synchronize()
+        repeat_same = torch.equal(out.view(torch.int16), out2.view(torch.int16))
         torch.cuda.synchronize()
         # single-GPU reference over all ranks' tokens
         ref_layer = pkg.MoELayer(pkg.W4A8Weights(*[t.to(dev) for t in full.w13]),
@@ -59,7 +66,7 @@ def _worker(rank, world, port, q, zipf):
         start = sum(t.x.shape[0] for t in toks[:rank])
         ref = ref[start:start + T]
         torch.cuda.synchronize()
-        same = torch.equal(out.view(torch.int16), ref.view(torch.int16))
+        same = torch.equal(out.view(torch.int16), ref.view(torch.int16)) and repeat_same
         q.put((rank, "ok", bool(same), float((out.float() - ref.float()).abs().max()), pkg.device_status()))
         dist.barrier()
         dist.destroy_process_group()
@@ -67,14 +74,15 @@ def _worker(rank, world, port, q, zipf):
         q.put((rank, "error", traceback.format_exc()[-600:]))
 
 
+@pytest.mark.parametrize("transport", ["p2p", "nccl"])
 @pytest.mark.parametrize("zipf", [0.0, 1.2])
-def test_ep_two_gpus_matches_single_gpu(zipf):
+def test_ep_two_gpus_matches_single_gpu(zipf, transport):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, zipf)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, zipf, transport)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
