@@ -48,6 +48,8 @@ SIGNATURES = {
     "w4a8_ep_return": (ctypes.c_int, [_p, _i64, _i64, _p, _p, _i64, _i64, _p, _i64, _p]),
     "w4a8_act_quant": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "w4a8_quant_scatter": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _i64, _p, _p, _p]),
+    "w4a8_router_topk": (ctypes.c_int, [_p, _i64, _i64, _i64, _i64, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _i64,
+                                        _p, _p]),
     "w4a8_moe_align_workspace_size": (_sz, [_i64, _i64, _i64]),
     "w4a8_moe_align": (ctypes.c_int, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),
     "w4a8_silu_mul_requant": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _p, _p]),

@@ -69,10 +69,8 @@ namespace {
 // (Dest: LocalRows here, the peer receive buffers of ep_p2p.cu for the
 // expert-parallel dispatch).
 template <class Dest>
-__global__ void __launch_bounds__(kQThreads)
-act_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride0, int H, const Dest dest) {
-  __shared__ float red[32];
-  const int t = blockIdx.x;
+__device__ __forceinline__ void quant_row(const __nv_bfloat16* __restrict__ x, int64_t x_stride0, int H,
+                                          const Dest& dest, int t, float* red) {
   const __nv_bfloat16* xr = x + static_cast<int64_t>(t) * x_stride0;
   const bool vec = ((H & 7) == 0) && ((reinterpret_cast<uintptr_t>(xr) & 15) == 0) &&
                    (H / 8 <= kQThreads * kQMaxVec);
@@ -138,7 +136,95 @@ act_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride0, int H, 
   }
 }
 
+template <class Dest>
+__global__ void __launch_bounds__(kQThreads)
+act_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride0, int H, const Dest dest) {
+  __shared__ float red[32];
+  quant_row(x, x_stride0, H, dest, blockIdx.x, red);
+}
+
+// Router of one token, run by one warp: scores (softmax or sigmoid of the E
+// logits), the top-k experts by score in descending order, their weights
+// renormalised to sum to 1.  Follows the routing of the benchmark inputs
+// (softmax | sigmoid -> torch.topk -> w / w.sum()).  Experts are ranked by
+// logit, which orders them exactly as their scores do (both maps are
+// increasing), with ties going to the lower expert index, so the selection
+// does not depend on how the scores round.  Lane l holds logits l, l + 32, ...
+template <int kPerLane>
+__device__ __forceinline__ void route_token(const RouterArgs& r, int t, int lane) {
+  const float* lg = r.logits + static_cast<int64_t>(t) * r.logits_stride0;
+  float v[kPerLane];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kPerLane; ++j) {
+    const int e = lane + 32 * j;
+    v[j] = e < r.E ? __ldg(lg + e) : -INFINITY;
+    mx = fmaxf(mx, v[j]);
+  }
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, d));
+  float denom = 1.f;   // softmax: sum of exp(logit - max) over all experts
+  if (r.scoring == 0) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j)
+      if (lane + 32 * j < r.E) s = __fadd_rn(s, expf(v[j] - mx));
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, d));
+    denom = s;
+  }
+  uint32_t taken = 0;   // bit j: this lane's logit j already selected
+  float my_w = 0.f, wsum = 0.f;
+  int my_id = 0;
+  for (int k = 0; k < r.topk; ++k) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j) {
+      const int e = lane + 32 * j;
+      if (e < r.E && !((taken >> j) & 1u) && (v[j] > best || bi == 0x7fffffff)) { best = v[j]; bi = e; }
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, d);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, d);
+      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    const float score = r.scoring == 0 ? __fdiv_rn(expf(best - mx), denom) : __fdiv_rn(1.f, 1.f + expf(-best));
+    wsum = __fadd_rn(wsum, score);
+    if (lane == k) { my_w = score; my_id = bi; }
+  }
+  if (lane < r.topk) {
+    const int64_t o = static_cast<int64_t>(t) * r.topk + lane;
+    r.ids[o] = my_id;
+    r.weights[o] = r.renormalize ? __fdiv_rn(my_w, wsum) : my_w;
+  }
+}
+
+// Router + quantisation of one token per CTA: warp 0 routes the token while
+// the CTA quantises its hidden row (when x is given) into row t of x_q.
+template <int kPerLane>
+__global__ void __launch_bounds__(kQThreads)
+router_quant_kernel(const RouterArgs r, const __nv_bfloat16* __restrict__ x, int64_t x_stride0, int H,
+                    const LocalRows dest) {
+  __shared__ float red[32];
+  if (threadIdx.x < 32) route_token<kPerLane>(r, blockIdx.x, threadIdx.x);
+  if (x != nullptr) quant_row(x, x_stride0, H, dest, blockIdx.x, red);
+}
+
 }  // namespace
+
+cudaError_t launch_router(const RouterArgs& r, int T, const __nv_bfloat16* x, int64_t x_stride0, int H, int8_t* q,
+                          int64_t q_stride0, float* s, cudaStream_t stream) {
+  if (T <= 0) return cudaSuccess;
+  const LocalRows dest{q, q_stride0, s, nullptr, 1};
+  if (r.E <= 256)
+    router_quant_kernel<8><<<T, kQThreads, 0, stream>>>(r, x, x_stride0, H, dest);
+  else
+    router_quant_kernel<32><<<T, kQThreads, 0, stream>>>(r, x, x_stride0, H, dest);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_act_quant(const __nv_bfloat16* x, int64_t x_stride0, int T, int H, int8_t* q,
                              int64_t q_stride0, float* s, const int32_t* rows_out, int topk,

@@ -299,6 +299,27 @@ int w4a8_act_quant(const void* x, int64_t x_stride0, int64_t T, int64_t H, int8_
   return e == cudaSuccess ? W4A8_OK : cuda_fail(e, "act_quant launch");
 }
 
+int w4a8_router_topk(const float* logits, int64_t logits_stride0, int64_t T, int64_t E, int64_t topk,
+                     int32_t scoring, int32_t renormalize, int32_t* topk_ids, float* topk_weights,
+                     const void* x, int64_t x_stride0, int64_t H, int8_t* x_q, int64_t q_stride0,
+                     float* x_scale, void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+  if (T < 0 || T > INT32_MAX || E <= 0 || E > kRouterMaxExperts || topk <= 0 || topk > E ||
+      topk > kRouterMaxTopk || (scoring != 0 && scoring != 1) || logits_stride0 < E)
+    return fail(W4A8_ERR_INVALID, "bad router arguments T=%lld E=%lld topk=%lld scoring=%d", (long long)T,
+                (long long)E, (long long)topk, (int)scoring);
+  if (x != nullptr && (H <= 0 || H > INT32_MAX || x_stride0 < H || q_stride0 < H || x_q == nullptr ||
+                       x_scale == nullptr))
+    return fail(W4A8_ERR_INVALID, "bad quantisation arguments H=%lld", (long long)H);
+  if (T == 0) return W4A8_OK;
+  if (logits == nullptr || topk_ids == nullptr || topk_weights == nullptr) return fail(W4A8_ERR_INVALID, "null pointer");
+  const RouterArgs r{logits, logits_stride0, (int)E, (int)topk, (int)scoring, renormalize != 0 ? 1 : 0,
+                     topk_ids, topk_weights};
+  cudaError_t e = launch_router(r, (int)T, static_cast<const __nv_bfloat16*>(x), x_stride0, (int)H, x_q, q_stride0,
+                                x_scale, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? W4A8_OK : cuda_fail(e, "router launch");
+}
+
 int w4a8_quant_scatter(const void* x, int64_t x_stride0, int64_t T, int64_t H, const int32_t* inv_pos,
                        int64_t topk, int8_t* x_sorted, float* xs_sorted, void* stream) {
   if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");

@@ -46,6 +46,9 @@ constexpr int kGvMaxStages = 4;   // ring depth per CTA
 constexpr int kGvTargetW = 32 * 1024;                  // preferred weight bytes per stage
 constexpr int kGvMaxRB = 32;                           // rows per block
 constexpr int kGvSmemBudget = 110 * 1024;   // two CTAs per SM when it fits
+constexpr int kGvPlain = 0;      // epilogue modes: bf16 rows
+constexpr int kGvCombine = 1;    // fused top-k combine into fp32 token rows
+constexpr int kGvPartials = 2;   // bf16 rows and the int32 per-group partials
 constexpr int kWrapZero = -112;   // z >= kWrapZero: nib - z stays inside int8 for every nibble
 
 struct GvParams {
@@ -187,7 +190,7 @@ __device__ __forceinline__ void partials_wrap(const uint8_t* wg, const uint8_t* 
 // finishes the output.  NG groups of a lane are in flight at once.  HALF:
 // rows with at most 16 K-groups are taken two per warp, one per half-warp
 // (`write` is false for a half-warp without a row of its own).
-template <int R, int GS, int NG, bool HALF, bool kCombine>
+template <int R, int GS, int NG, bool HALF, int kMode>
 __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const TokenTile& tt, int G, int lane,
                                        bool write) {
   constexpr int kRot = GS == 128 ? 1 : 2;       // lane -> chunk rotation (conflict-free quarter warps)
@@ -245,8 +248,8 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         acc[r] = fmaf(static_cast<float>(p[n][r]), ws, acc[r]);
-        if (a.partials != nullptr && write)
-          a.partials[(static_cast<int64_t>(g[n]) * a.M_total + j.m0 + r) * a.N + j.n] = p[n][r];
+        if constexpr (kMode == kGvPartials)
+          if (write) a.partials[(static_cast<int64_t>(g[n]) * a.M_total + j.m0 + r) * a.N + j.n] = p[n][r];
       }
     }
   }
@@ -257,7 +260,7 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const
     for (int d = kSpan / 2; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
     if (l == 0 && write) {
       const int m = j.m0 + r;
-      if constexpr (kCombine) {
+      if constexpr (kMode == kGvCombine) {
         store_output(a, m, j.n, v);   // fused top-k combine into the token's fp32 row
       } else {
         a.out[static_cast<int64_t>(m) * a.out_stride0 + static_cast<int64_t>(j.n) * a.out_stride1] =
@@ -366,9 +369,10 @@ __device__ __noinline__ void cost_balanced_range(int E, int NB, const int* cnt, 
 
 // kShort: every row has at most 16 K-groups and a warp takes two rows, one
 // per half-warp (a separate instantiation, so neither mode's register
-// allocation pays for the other's code).  kCombine: the fused top-k combine
-// store (also its own instantiation).
-template <bool kShort, bool kCombine>
+// allocation pays for the other's code).  kMode: plain bf16 rows, the fused
+// top-k combine store, or bf16 rows plus the int32 partials export (each its
+// own instantiation, so the plain kernel carries neither).
+template <bool kShort, int kMode>
 __global__ void __launch_bounds__(kGvThreads, 2)
 gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
   extern __shared__ unsigned char smem_raw[];
@@ -473,17 +477,17 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
                            static_cast<int64_t>(tile.e) * a.N + n0 + ri};
           if (a.gs == 128) {
             switch (tile.rows) {   // warp-uniform: the tile's token count
-              case 1: gv_row<1, 128, 1, true, kCombine>(a, job, tt, G, lane, write); break;
-              case 2: gv_row<2, 128, 1, true, kCombine>(a, job, tt, G, lane, write); break;
-              case 3: gv_row<3, 128, 1, true, kCombine>(a, job, tt, G, lane, write); break;
-              default: gv_row<4, 128, 1, true, kCombine>(a, job, tt, G, lane, write); break;
+              case 1: gv_row<1, 128, 1, true, kMode>(a, job, tt, G, lane, write); break;
+              case 2: gv_row<2, 128, 1, true, kMode>(a, job, tt, G, lane, write); break;
+              case 3: gv_row<3, 128, 1, true, kMode>(a, job, tt, G, lane, write); break;
+              default: gv_row<4, 128, 1, true, kMode>(a, job, tt, G, lane, write); break;
             }
           } else {
             switch (tile.rows) {
-              case 1: gv_row<1, 64, 1, true, kCombine>(a, job, tt, G, lane, write); break;
-              case 2: gv_row<2, 64, 1, true, kCombine>(a, job, tt, G, lane, write); break;
-              case 3: gv_row<3, 64, 1, true, kCombine>(a, job, tt, G, lane, write); break;
-              default: gv_row<4, 64, 1, true, kCombine>(a, job, tt, G, lane, write); break;
+              case 1: gv_row<1, 64, 1, true, kMode>(a, job, tt, G, lane, write); break;
+              case 2: gv_row<2, 64, 1, true, kMode>(a, job, tt, G, lane, write); break;
+              case 3: gv_row<3, 64, 1, true, kMode>(a, job, tt, G, lane, write); break;
+              default: gv_row<4, 64, 1, true, kMode>(a, job, tt, G, lane, write); break;
             }
           }
         }
@@ -494,17 +498,17 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
                            static_cast<int64_t>(tile.e) * a.N + n0 + rr};
           if (a.gs == 128) {
             switch (tile.rows) {   // warp-uniform: the tile's token count
-              case 1: gv_row<1, 128, 2, false, kCombine>(a, job, tt, G, lane, true); break;
-              case 2: gv_row<2, 128, 2, false, kCombine>(a, job, tt, G, lane, true); break;
-              case 3: gv_row<3, 128, 1, false, kCombine>(a, job, tt, G, lane, true); break;
-              default: gv_row<4, 128, 1, false, kCombine>(a, job, tt, G, lane, true); break;
+              case 1: gv_row<1, 128, 2, false, kMode>(a, job, tt, G, lane, true); break;
+              case 2: gv_row<2, 128, 2, false, kMode>(a, job, tt, G, lane, true); break;
+              case 3: gv_row<3, 128, 1, false, kMode>(a, job, tt, G, lane, true); break;
+              default: gv_row<4, 128, 1, false, kMode>(a, job, tt, G, lane, true); break;
             }
           } else {
             switch (tile.rows) {
-              case 1: gv_row<1, 64, 2, false, kCombine>(a, job, tt, G, lane, true); break;
-              case 2: gv_row<2, 64, 2, false, kCombine>(a, job, tt, G, lane, true); break;
-              case 3: gv_row<3, 64, 1, false, kCombine>(a, job, tt, G, lane, true); break;
-              default: gv_row<4, 64, 1, false, kCombine>(a, job, tt, G, lane, true); break;
+              case 1: gv_row<1, 64, 2, false, kMode>(a, job, tt, G, lane, true); break;
+              case 2: gv_row<2, 64, 2, false, kMode>(a, job, tt, G, lane, true); break;
+              case 3: gv_row<3, 64, 1, false, kMode>(a, job, tt, G, lane, true); break;
+              default: gv_row<4, 64, 1, false, kMode>(a, job, tt, G, lane, true); break;
             }
           }
         }
@@ -555,8 +559,11 @@ cudaError_t launch_gemm_gemv(const GemmArgs& a, cudaStream_t stream) {
   }
   const size_t smem = fixed + gp.stages * stage_bytes;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  auto kernel = a.comb_out != nullptr ? (G <= 16 ? gemm_gemv_kernel<true, true> : gemm_gemv_kernel<false, true>)
-                                      : (G <= 16 ? gemm_gemv_kernel<true, false> : gemm_gemv_kernel<false, false>);
+  auto kernel = a.comb_out != nullptr
+                     ? (G <= 16 ? gemm_gemv_kernel<true, kGvCombine> : gemm_gemv_kernel<false, kGvCombine>)
+                 : a.partials != nullptr
+                     ? (G <= 16 ? gemm_gemv_kernel<true, kGvPartials> : gemm_gemv_kernel<false, kGvPartials>)
+                     : (G <= 16 ? gemm_gemv_kernel<true, kGvPlain> : gemm_gemv_kernel<false, kGvPlain>);
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 0;

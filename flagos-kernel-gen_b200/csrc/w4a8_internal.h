@@ -70,6 +70,23 @@ int* device_status_ptr();  // per-device status word (static __device__ storage)
 // the calling thread) current in the library's own runtime.
 cudaError_t bind_stream_device(void* stream);
 
+// Router of a token batch (scores, top-k, renormalisation) on the device.
+struct RouterArgs {
+  const float* logits;      // [T, E], row stride logits_stride0
+  int64_t logits_stride0;
+  int E, topk;
+  int scoring;              // 0 softmax, 1 sigmoid
+  int renormalize;          // weights divided by their sum over the k selected
+  int32_t* ids;             // [T, topk]
+  float* weights;           // [T, topk]
+};
+constexpr int kRouterMaxExperts = 1024;
+constexpr int kRouterMaxTopk = 32;
+// Routes T tokens and, with x given, quantises each token's hidden row into
+// row t of q (the act-quant convention) in the same launch.
+cudaError_t launch_router(const RouterArgs& r, int T, const __nv_bfloat16* x, int64_t x_stride0, int H, int8_t* q,
+                          int64_t q_stride0, float* s, cudaStream_t stream);
+
 // Largest padded-block size the align entry points accept: the padded
 // outputs hold T*topk + E*(block_size-1) entries, which must stay well inside
 // the kernels' 32-bit index range.

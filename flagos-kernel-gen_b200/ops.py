@@ -196,6 +196,42 @@ def act_quant(x: torch.Tensor, x_q: torch.Tensor | None = None, x_scale: torch.T
     return x_q, x_scale
 
 
+def router_topk(logits: torch.Tensor, topk: int, scoring: str = "softmax", renormalize: bool = True,
+                x: torch.Tensor | None = None):
+    """Router on the device: scores (``"softmax"`` or ``"sigmoid"`` of fp32
+    ``logits`` [T, E]), the ``topk`` experts by score in descending order,
+    weights renormalised to sum to 1 -> (ids int32 [T, k], weights fp32 [T, k]).
+    With bf16 ``x`` [T, H] the same launch also quantises every token row as
+    ``act_quant`` does and returns (ids, weights, x_q, x_scale).  Ranking is
+    by logit (the scores' order), ties to the lower expert index."""
+    dev = _require_cuda(logits)
+    if logits.dtype != torch.float32 or logits.dim() != 2:
+        raise TypeError("logits must be a 2-D float32 tensor")
+    if scoring not in ("softmax", "sigmoid"):
+        raise ValueError("scoring must be 'softmax' or 'sigmoid'")
+    if logits.stride(1) != 1:
+        logits = logits.contiguous()
+    T, E = logits.shape
+    ids = torch.empty((T, topk), dtype=torch.int32, device=dev)
+    w = torch.empty((T, topk), dtype=torch.float32, device=dev)
+    xq = xs = None
+    xp, xstride, H, qp, qstride, sp = None, 0, 0, None, 0, None
+    if x is not None:
+        if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[0] != T or x.device != dev:
+            raise TypeError("x must be a bfloat16 [T, H] tensor on the logits' device")
+        if x.stride(1) != 1:
+            x = x.contiguous()
+        H = x.shape[1]
+        xq = torch.empty((T, H), dtype=torch.int8, device=dev)
+        xs = torch.empty((T,), dtype=torch.float32, device=dev)
+        xp, xstride, qp, qstride, sp = x.data_ptr(), x.stride(0), xq.data_ptr(), xq.stride(0), xs.data_ptr()
+    rc = _lib.load().w4a8_router_topk(logits.data_ptr(), logits.stride(0), T, E, topk,
+                                      0 if scoring == "softmax" else 1, 1 if renormalize else 0,
+                                      ids.data_ptr(), w.data_ptr(), xp, xstride, H, qp, qstride, sp, _stream(dev))
+    _lib.check(rc, "router_topk")
+    return (ids, w) if x is None else (ids, w, xq, xs)
+
+
 class AlignResult(NamedTuple):
     expert_offsets: torch.Tensor   # int32 [E+1]
     sorted_ids: torch.Tensor       # int32 [R]

@@ -135,6 +135,24 @@ int w4a8_act_quant(const void* x, int64_t x_stride0, int64_t T, int64_t H, int8_
                    int64_t q_stride0, float* x_scale, void* stream);
 
 /*
+ * Router + top-k, optionally fused with the activation quantisation.  The
+ * reference takes routing as given (its entry point receives expert_offsets,
+ * docs/Task1.md:13); this is the routing its benchmark inputs use: scores =
+ * softmax (scoring 0) or sigmoid (scoring 1) of the logits, the topk experts
+ * by score in descending order (torch.topk), weights renormalised to sum to 1
+ * (renormalize != 0).  Experts are ranked by logit (the same order as their
+ * scores), ties to the lower expert index.
+ *   logits fp32 [T, E] (row stride logits_stride0), E <= 1024, topk <= min(E, 32)
+ *   topk_ids int32 [T, topk], topk_weights fp32 [T, topk] (contiguous)
+ *   x bf16 [T, H] (row stride x_stride0) or NULL: with x, also x_q int8 [T, H]
+ *   (row stride q_stride0) and x_scale fp32 [T] exactly as w4a8_act_quant.
+ */
+int w4a8_router_topk(const float* logits, int64_t logits_stride0, int64_t T, int64_t E, int64_t topk,
+                     int32_t scoring, int32_t renormalize, int32_t* topk_ids, float* topk_weights,
+                     const void* x, int64_t x_stride0, int64_t H, int8_t* x_q, int64_t q_stride0,
+                     float* x_scale, void* stream);
+
+/*
  * Fused quantise + dispatch: quantises token t once (as w4a8_act_quant) and
  * writes it to rows inv_pos[t*topk + j] (j < topk) of x_sorted / xs_sorted,
  * i.e. straight into expert-sorted order.  inv_pos comes from w4a8_moe_align;

@@ -176,6 +176,28 @@ def silu_mul_requant(h_bf16: torch.Tensor):
     return quant_rows(y.numpy())
 
 
+# ----------------------------------------------------------------------------- router
+def route_topk(logits, topk: int, scoring: str, renormalize: bool = True):
+    """Routing of the benchmark inputs (softmax or sigmoid of fp32 logits [T, E]
+    -> top-k -> weights / their sum; SURVEY's router row N5, the reference takes
+    routing as given).  Ranking: descending logit, ties to the lower expert
+    index (the scores are increasing functions of the logits, so this is their
+    top-k order).  Scores are fp32; returns (ids int32 [T, k], weights fp32 [T, k])."""
+    lg = np.asarray(_np(logits), dtype=np.float32)
+    T, E = lg.shape
+    order = np.lexsort((np.broadcast_to(np.arange(E), (T, E)), -lg), axis=-1)[:, :topk]
+    top = np.take_along_axis(lg, order, axis=-1)
+    if scoring == "softmax":
+        mx = lg.max(axis=-1, keepdims=True)
+        den = np.exp(lg - mx, dtype=np.float32).sum(axis=-1, keepdims=True, dtype=np.float32)
+        sc = (np.exp(top - mx, dtype=np.float32) / den).astype(np.float32)
+    else:
+        sc = (np.float32(1.0) / (np.float32(1.0) + np.exp(-top, dtype=np.float32))).astype(np.float32)
+    if renormalize:
+        sc = (sc / sc.sum(axis=-1, keepdims=True, dtype=np.float32)).astype(np.float32)
+    return order.astype(np.int32), sc
+
+
 # ----------------------------------------------------------------------------- align / combine
 def moe_align(topk_ids, E: int, block_size: int):
     """Stable counting sort of flat (token, slot) indices by expert.

@@ -107,3 +107,24 @@ def test_layer_on_a_token_subset_equals_the_full_layer(pkg, O, seed, zipf):
     toks = [5, 0, 63, 7, 17]
     sub = O.moe_layer_tokens(inp.x, ids, inp.topk_weights, inp.w13, inp.w2, 128, toks)
     np.testing.assert_array_equal(O.bf16_bits(full[toks]), O.bf16_bits(sub))
+
+
+@pytest.mark.parametrize("scoring,E,k,T", [("softmax", 8, 2, 64), ("sigmoid", 256, 8, 300), ("softmax", 128, 8, 97),
+                                           ("sigmoid", 3, 3, 5)])
+def test_router_restatement_matches_the_benchmark_router(pkg, O, scoring, E, k, T):
+    """The oracle's router (ranking by logit, ties to the lower index) picks the
+    same experts in the same order as the torch router that makes the benchmark
+    inputs (scores -> torch.topk -> renormalise), with weights within a few ulps."""
+    g = pkg.workloads.make_generator(T + E)
+    logits = torch.randn((T, E), generator=g, dtype=torch.float32)
+    ids_t, w_t = pkg.workloads.route(logits, k, scoring)
+    ids_o, w_o = O.route_topk(logits, k, scoring)
+    np.testing.assert_array_equal(ids_o, ids_t.numpy())
+    np.testing.assert_allclose(w_o, w_t.numpy(), rtol=2e-6, atol=0)
+
+
+def test_router_ties_go_to_the_lower_index(O):
+    logits = np.array([[1.0, 3.0, 3.0, -np.inf, 2.0, 3.0]], dtype=np.float32)
+    ids, w = O.route_topk(logits, 4, "sigmoid")
+    np.testing.assert_array_equal(ids, [[1, 2, 5, 4]])
+    assert abs(float(w.sum()) - 1.0) < 1e-6
