@@ -460,6 +460,35 @@ def north_star_targets(pkg, layer, cfg, dev, steps, peaks):
     return out
 
 
+def router_stage(pkg, cfg, T, dev, steps, peaks):
+    """The router + top-k kernel fused with the token quantisation, at the
+    layer's token count: CUDA-event time per launch, HBM fraction of its
+    algorithmic bytes (logits and bf16 rows in; int8 rows, scales, ids and
+    weights out), and its expert ids against the oracle on sampled tokens."""
+    from oracle import w4a8_oracle as O
+    W = pkg.workloads
+    g = W.make_generator(5, dev)
+    logits = torch.randn((T, cfg.experts), generator=g, device=dev, dtype=torch.float32)
+    x = torch.randn((T, cfg.hidden), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    for _ in range(3):
+        pkg.router_topk(logits, cfg.topk, cfg.scoring, x=x)
+    evs = []
+    for _ in range(max(steps, 5)):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        res = pkg.router_topk(logits, cfg.topk, cfg.scoring, x=x)
+        b.record()
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+    byts = T * cfg.experts * 4 + T * cfg.hidden * 2 + T * cfg.hidden + T * 4 + T * cfg.topk * 8
+    rows = torch.linspace(0, T - 1, steps=min(T, 64)).long()
+    ids_o, _ = O.route_topk(logits[rows].cpu(), cfg.topk, cfg.scoring)
+    return {"kernel": "router_quant_kernel", "tokens": T, "ms_per_launch": ms,
+            "hbm_frac": byts / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes": byts,
+            "ids_match_oracle": bool((res[0][rows].cpu().numpy() == ids_o).all())}
+
+
 def routing_variant(pkg, layer, cfg, T, rank, world, dev, steps):
     """The other routing of the same layer (Zipf(1.2) popularity for a uniform
     workload, uniform for a Zipf one): tokens/s (max over ranks) and the load
@@ -662,10 +691,12 @@ def main():
         roof["down_ms_per_launch"] = dn_ms
         roof["down_int8_frac"] = W.gemm_ops(R, cfg.hidden, cfg.inter) / (dn_ms * 1e-3) / 1e12 / int8_peak
 
-    targets = variant = None
+    targets = variant = router = None
     if not args.no_extras:
         if world == 1 and cfg.name.startswith("deepseek") and cfg.ffn:
             targets = north_star_targets(pkg, layer, W.CONFIGS["deepseek"], dev, max(5, args.steps), peaks)
+        if world == 1:
+            router = router_stage(pkg, cfg, T, dev, args.steps, peaks)
         variant = routing_variant(pkg, layer, cfg, T, rank, world, dev, args.steps)
 
     cpu = None
@@ -684,6 +715,7 @@ def main():
                 "gpu_launches": args.steps * layer.launches_per_forward(),
                 "roofline": roof, "cpu_baseline": cpu, "clocks": clocks, "device_status": status,
                 "parity": parity, "stages_ms": stages, "targets": targets, "routing_variant": variant,
+                "router": router,
                 "active_experts": active, "routed_rows": R}
         print(json.dumps(line), flush=True)
     if world > 1:

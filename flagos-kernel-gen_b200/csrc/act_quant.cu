@@ -202,15 +202,21 @@ __device__ __forceinline__ void route_token(const RouterArgs& r, int t, int lane
   }
 }
 
-// Router + quantisation of one token per CTA: warp 0 routes the token while
-// the CTA quantises its hidden row (when x is given) into row t of x_q.
+// Router + quantisation of kRouterTokens tokens per CTA: each warp routes
+// one of them (a CTA per token routed by one warp was bound by CTA launches
+// and the serial top-k: 110 us for 16384 tokens), then the CTA quantises
+// their hidden rows one after another (when x is given) into rows t of x_q.
+constexpr int kRouterTokens = kQThreads / 32;
 template <int kPerLane>
 __global__ void __launch_bounds__(kQThreads)
-router_quant_kernel(const RouterArgs r, const __nv_bfloat16* __restrict__ x, int64_t x_stride0, int H,
+router_quant_kernel(const RouterArgs r, int T, const __nv_bfloat16* __restrict__ x, int64_t x_stride0, int H,
                     const LocalRows dest) {
   __shared__ float red[32];
-  if (threadIdx.x < 32) route_token<kPerLane>(r, blockIdx.x, threadIdx.x);
-  if (x != nullptr) quant_row(x, x_stride0, H, dest, blockIdx.x, red);
+  const int t0 = blockIdx.x * kRouterTokens;
+  const int mine = t0 + (threadIdx.x >> 5);
+  if (mine < T) route_token<kPerLane>(r, mine, threadIdx.x & 31);
+  if (x != nullptr)
+    for (int t = t0; t < T && t < t0 + kRouterTokens; ++t) quant_row(x, x_stride0, H, dest, t, red);
 }
 
 }  // namespace
@@ -219,10 +225,11 @@ cudaError_t launch_router(const RouterArgs& r, int T, const __nv_bfloat16* x, in
                           int64_t q_stride0, float* s, cudaStream_t stream) {
   if (T <= 0) return cudaSuccess;
   const LocalRows dest{q, q_stride0, s, nullptr, 1};
+  const int grid = (T + kRouterTokens - 1) / kRouterTokens;
   if (r.E <= 256)
-    router_quant_kernel<8><<<T, kQThreads, 0, stream>>>(r, x, x_stride0, H, dest);
+    router_quant_kernel<8><<<grid, kQThreads, 0, stream>>>(r, T, x, x_stride0, H, dest);
   else
-    router_quant_kernel<32><<<T, kQThreads, 0, stream>>>(r, x, x_stride0, H, dest);
+    router_quant_kernel<32><<<grid, kQThreads, 0, stream>>>(r, T, x, x_stride0, H, dest);
   return cudaGetLastError();
 }
 

@@ -42,6 +42,7 @@ namespace {
 constexpr int kGvConsumers = 8;
 constexpr int kGvThreads = (kGvConsumers + 1) * 32;   // + producer warp
 constexpr int kGvRows = kGemvMaxTokens;                // tokens per pass
+static_assert(kGvRows <= 4, "the token-scale slot in shared memory holds 4 floats");
 constexpr int kGvMaxStages = 4;   // ring depth per CTA
 constexpr int kGvTargetW = 32 * 1024;                  // preferred weight bytes per stage
 constexpr int kGvMaxRB = 32;                           // rows per block
@@ -87,6 +88,7 @@ struct TokenTile {
   const uint8_t* xe;   // [kGvRows][K/2] even-k bytes, 16 per 32-value chunk
   const uint8_t* xo;   // [kGvRows][K/2] odd-k bytes
   const int* sx;       // [kGvRows][G] group sums
+  const float* xsc;    // [kGvRows] token scales of the rows
 };
 
 struct RowJob {
@@ -264,7 +266,7 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const
         store_output(a, m, j.n, v);   // fused top-k combine into the token's fp32 row
       } else {
         a.out[static_cast<int64_t>(m) * a.out_stride0 + static_cast<int64_t>(j.n) * a.out_stride1] =
-            __float2bfloat16_rn(v * __ldg(a.x_scale + m));
+            __float2bfloat16_rn(v * tt.xsc[r]);
       }
     }
   }
@@ -273,7 +275,11 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const
 // Stages the token rows [m0, m0 + rows) of x_q: per 32-value chunk the 16
 // even-k bytes and the 16 odd-k bytes, and per K-group the sum of its
 // values.  Called by all consumer threads between two consumer barriers.
-__device__ __forceinline__ void stage_tokens(const GemmArgs& a, int m0, int rows, uint8_t* xe, uint8_t* xo, int* sx) {
+__device__ __forceinline__ void stage_tokens(const GemmArgs& a, int m0, int rows, uint8_t* xe, uint8_t* xo, int* sx,
+                                             float* xsc) {
+  // token scales: read once per token block here instead of by every row's
+  // store (a global load at the end of each row's chain)
+  if (threadIdx.x < rows) xsc[threadIdx.x] = __ldg(a.x_scale + m0 + threadIdx.x);
   const int half_k = a.K >> 1;
   const int G = a.K / a.gs;
   const int cpg = a.gs / 32;
@@ -384,7 +390,8 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
   uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(s_sx) + gp.sx_bytes);
   uint64_t* empty = full + kGvMaxStages;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kGvMaxStages);
-  int* sched_mem = const_cast<int*>(reinterpret_cast<volatile int*>(abort_flag)) + 4;
+  float* s_xsc = const_cast<float*>(reinterpret_cast<volatile float*>(abort_flag + 4));   // [kGvRows]
+  int* sched_mem = const_cast<int*>(reinterpret_cast<volatile int*>(abort_flag)) + 8;
 
   const int warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
@@ -438,7 +445,7 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
     }
   } else {
     // ------------------------------------------------------------ consumers
-    const TokenTile tt{s_xe, s_xo, s_sx};
+    const TokenTile tt{s_xe, s_xo, s_sx, s_xsc};
     int cur_m0 = -1, cur_rows = 0;
     int stage = 0;
     uint32_t phase = 0;
@@ -451,7 +458,7 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
       const Tile tile = walk.cur;
       if (tile.m0 != cur_m0 || tile.rows != cur_rows) {   // uniform over the consumers
         consumers_sync();                                 // nobody still reads the old rows
-        stage_tokens(a, tile.m0, tile.rows, s_xe, s_xo, s_sx);
+        stage_tokens(a, tile.m0, tile.rows, s_xe, s_xo, s_sx, s_xsc);
         consumers_sync();
         cur_m0 = tile.m0;
         cur_rows = tile.rows;
@@ -548,7 +555,7 @@ cudaError_t launch_gemm_gemv(const GemmArgs& a, cudaStream_t stream) {
   gp.x_bytes = kGvRows * a.K;                    // K is a multiple of 64: both halves stay 16-byte aligned
   gp.sx_bytes = ((kGvRows * G * 4 + 15) / 16) * 16;
   const size_t stage_bytes = gp.stage_w + gp.ws_bytes + gp.z_bytes;
-  const size_t fixed = 128 + gp.x_bytes + gp.sx_bytes + 2 * kGvMaxStages * 8 + 16 + sizeof(int) * 3 * (a.E + 1) + 8 +
+  const size_t fixed = 128 + gp.x_bytes + gp.sx_bytes + 2 * kGvMaxStages * 8 + 32 + sizeof(int) * 3 * (a.E + 1) + 8 +
                        sizeof(long long) * (a.E + 1);
   // deepest ring that keeps two CTAs per SM, else the deepest that fits one
   gp.stages = kGvMaxStages;
