@@ -149,6 +149,26 @@ ep_return_kernel(const __nv_bfloat16* __restrict__ y, int64_t y_stride0, int H, 
   }
 }
 
+// Return addresses of the received rows: row r < *total_rows of this rank's
+// receive order goes to row f of its sender's yhome (src[r] = sender * tk_max
+// + f); rows past the count get 0.  A grouped GEMM given this table
+// (w4a8_group_gemm_moe_rows) stores its results straight into the senders'
+// buffers, so no separate return pass runs.
+__global__ void ep_row_addr_kernel(const int32_t* __restrict__ src, const int32_t* __restrict__ total_rows, int cap,
+                                   int64_t tk_max, int64_t row_bytes, uint8_t* const* peers, int64_t yhome_off,
+                                   uint64_t* __restrict__ out_rows) {
+  const int rows = *total_rows;
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < cap; r += gridDim.x * blockDim.x) {
+    uint64_t a = 0;
+    if (r < rows) {
+      const int64_t code = src[r];
+      const int snd = static_cast<int>(code / tk_max);
+      a = reinterpret_cast<uint64_t>(peers[snd] + yhome_off + (code - snd * tk_max) * row_bytes);
+    }
+    out_rows[r] = a;
+  }
+}
+
 int ep_fail(int code, const char* msg) {
   set_last_error(msg);
   return code;
@@ -226,6 +246,22 @@ int w4a8_ep_return(const void* y, int64_t y_stride0, int64_t H, const int32_t* s
   ep_return_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(y), y_stride0, (int)H, src, total_rows, tk_max,
       reinterpret_cast<uint8_t* const*>(peers), yhome_off);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? W4A8_OK : ep_fail(W4A8_ERR_CUDA, cudaGetErrorString(e));
+}
+
+int w4a8_ep_row_addresses(const int32_t* src, const int32_t* total_rows, int64_t cap_rows, int64_t H,
+                          int64_t tk_max, void* const* peers, int64_t yhome_off, uint64_t* out_rows, void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return ep_fail(W4A8_ERR_CUDA, cudaGetErrorString(be));
+  if (cap_rows < 0 || cap_rows > INT32_MAX || H <= 0 || tk_max <= 0)
+    return ep_fail(W4A8_ERR_INVALID, "w4a8_ep_row_addresses: bad sizes");
+  if (cap_rows == 0) return W4A8_OK;
+  if (src == nullptr || total_rows == nullptr || peers == nullptr || out_rows == nullptr)
+    return ep_fail(W4A8_ERR_INVALID, "w4a8_ep_row_addresses: null pointer");
+  const int64_t blocks = (cap_rows + 255) / 256;
+  ep_row_addr_kernel<<<static_cast<int>(blocks < 1184 ? blocks : 1184), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      src, total_rows, static_cast<int>(cap_rows), tk_max, H * 2, reinterpret_cast<uint8_t* const*>(peers),
+      yhome_off, out_rows);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? W4A8_OK : ep_fail(W4A8_ERR_CUDA, cudaGetErrorString(e));
 }

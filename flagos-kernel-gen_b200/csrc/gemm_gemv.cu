@@ -50,6 +50,7 @@ constexpr int kGvSmemBudget = 110 * 1024;   // two CTAs per SM when it fits
 constexpr int kGvPlain = 0;      // epilogue modes: bf16 rows
 constexpr int kGvCombine = 1;    // fused top-k combine into fp32 token rows
 constexpr int kGvPartials = 2;   // bf16 rows and the int32 per-group partials
+constexpr int kGvRowAddr = 3;    // bf16 rows stored through a row-address table
 constexpr int kWrapZero = -112;   // z >= kWrapZero: nib - z stays inside int8 for every nibble
 
 struct GvParams {
@@ -264,6 +265,9 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const
       const int m = j.m0 + r;
       if constexpr (kMode == kGvCombine) {
         store_output(a, m, j.n, v);   // fused top-k combine into the token's fp32 row
+      } else if constexpr (kMode == kGvRowAddr) {
+        const uint64_t row = __ldg(a.out_rows + m);
+        if (row != 0) reinterpret_cast<__nv_bfloat16*>(row)[j.n] = __float2bfloat16_rn(v * tt.xsc[r]);
       } else {
         a.out[static_cast<int64_t>(m) * a.out_stride0 + static_cast<int64_t>(j.n) * a.out_stride1] =
             __float2bfloat16_rn(v * tt.xsc[r]);
@@ -568,6 +572,8 @@ cudaError_t launch_gemm_gemv(const GemmArgs& a, cudaStream_t stream) {
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   auto kernel = a.comb_out != nullptr
                      ? (G <= 16 ? gemm_gemv_kernel<true, kGvCombine> : gemm_gemv_kernel<false, kGvCombine>)
+                 : a.out_rows != nullptr
+                     ? (G <= 16 ? gemm_gemv_kernel<true, kGvRowAddr> : gemm_gemv_kernel<false, kGvRowAddr>)
                  : a.partials != nullptr
                      ? (G <= 16 ? gemm_gemv_kernel<true, kGvPartials> : gemm_gemv_kernel<false, kGvPartials>)
                      : (G <= 16 ? gemm_gemv_kernel<true, kGvPlain> : gemm_gemv_kernel<false, kGvPlain>);

@@ -61,6 +61,7 @@ namespace {
 constexpr int kModePlain = 0;      // bf16 rows (the reference's store)
 constexpr int kModeCombine = 1;    // fused top-k combine into fp32 token rows
 constexpr int kModePartials = 2;   // int32 per-group partials only, no scale math, no bf16 store
+constexpr int kModeRows = 3;       // bf16 rows stored through a row-address table (peer memory too)
 
 constexpr int kBW = 128;         // weight rows per tile (MMA M)
 constexpr int kBK = 128;         // K bytes per pipeline stage
@@ -604,6 +605,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
               // fused top-k combine: the weighted bf16 row result goes to its token's fp32 row
               store_output(a, m, n, lo);
               if (col + 1 < tile.rows) store_output(a, m + 1, n, hi);
+            } else if constexpr (kMode == kModeRows) {
+              store_row_addr(a, m, n, lo);
+              if (col + 1 < tile.rows) store_row_addr(a, m + 1, n, hi);
             } else {
               __nv_bfloat16* o = a.out + static_cast<int64_t>(m) * a.out_stride0 + static_cast<int64_t>(n) * a.out_stride1;
               *o = __float2bfloat16_rn(lo * __ldg(a.x_scale + m));
@@ -670,7 +674,8 @@ bool encode_2d_u8(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t ou
 template <class C, int kMode>
 cudaError_t launch_tc_kernel(const CUtensorMap& tm_x, const CUtensorMap& tm_xt, const CUtensorMap& tm_w,
                              const GemmArgs& a, cudaStream_t stream) {
-  static_assert(kMode == kModePlain || kMode == kModeCombine || kMode == kModePartials, "epilogue mode");
+  static_assert(kMode == kModePlain || kMode == kModeCombine || kMode == kModePartials || kMode == kModeRows,
+                "epilogue mode");
   // The setmaxnreg split relies on the launch's 512 x 128 registers; with
   // fewer, the epilogue's setmaxnreg.inc could wait forever, so refuse to
   // launch.
@@ -707,6 +712,7 @@ cudaError_t launch_tc_config(const CUtensorMap& tm_w, const GemmArgs& a, cudaStr
   // 1.4-1.9x slower).  With a partials export the plain kernel writes the
   // bf16 rows and a second launch of the same pipeline writes the partials.
   if (a.comb_out != nullptr) return launch_tc_kernel<C, kModeCombine>(tm_x, tm_xt, tm_w, a, stream);
+  if (a.out_rows != nullptr) return launch_tc_kernel<C, kModeRows>(tm_x, tm_xt, tm_w, a, stream);
   GemmArgs plain = a;
   plain.partials = nullptr;
   cudaError_t e = launch_tc_kernel<C, kModePlain>(tm_x, tm_xt, tm_w, plain, stream);

@@ -38,14 +38,27 @@ struct GemmArgs {
   const float* comb_w = nullptr;
   int comb_topk = 1;
   int64_t comb_stride = 0;
+  // Row-address store (out_rows != nullptr): row m's bf16 results go to the
+  // N contiguous elements at address out_rows[m] (0: row not stored) — e.g.
+  // straight into another GPU's buffer over NVLink peer memory.
+  const uint64_t* out_rows = nullptr;
 };
 
 #ifdef __CUDACC__
 // Output of row m, column n of a grouped GEMM: v is the fp32 group-scale sum,
 // the row's token scale is applied and the result rounded to bf16 (the
 // reference's store, docs/Task1.md:110-112); with the fused combine the
-// weighted bf16 value is added to the token's fp32 output row instead.
+// weighted bf16 value is added to the token's fp32 output row instead, and
+// with a row-address table it goes to that row's address.
+__device__ __forceinline__ void store_row_addr(const GemmArgs& a, int m, int n, float v) {
+  const uint64_t row = __ldg(a.out_rows + m);
+  if (row != 0) reinterpret_cast<__nv_bfloat16*>(row)[n] = __float2bfloat16_rn(v * __ldg(a.x_scale + m));
+}
 __device__ __forceinline__ void store_output(const GemmArgs& a, int m, int n, float v) {
+  if (a.out_rows != nullptr) {
+    store_row_addr(a, m, n, v);
+    return;
+  }
   const __nv_bfloat16 y = __float2bfloat16_rn(v * __ldg(a.x_scale + m));
   if (a.comb_out == nullptr) {
     a.out[static_cast<int64_t>(m) * a.out_stride0 + static_cast<int64_t>(n) * a.out_stride1] = y;

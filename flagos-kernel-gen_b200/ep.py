@@ -233,10 +233,14 @@ class P2PExpertParallelMoE:
     it.  Per forward, on every rank: align by global expert, exchange the
     per-expert row counts, dispatch, barrier, gate/up GEMM -> SiLU-mul
     requant -> down GEMM on the receive buffer, return, barrier, combine.
+    With ``fused_return`` (default) the last GEMM's epilogue stores every
+    result row straight into its sender's slot buffer over NVLink (a
+    row-address table built on the device after the dispatch), so the
+    return overlaps the GEMM instead of following it as a separate pass.
     """
 
     def __init__(self, w13_local: W4A8Weights, w2_local: W4A8Weights | None, num_experts: int, group_size: int,
-                 topk: int, max_tokens: int, group=None):
+                 topk: int, max_tokens: int, group=None, fused_return: bool = True):
         import torch.distributed._symmetric_memory as symm_mem
         from . import _lib
         self.group = group if group is not None else dist.group.WORLD
@@ -258,6 +262,7 @@ class P2PExpertParallelMoE:
         dev = w13_local.packed.device
         self.device = dev
         self.max_tokens = max_tokens
+        self.fused_return = fused_return
         self.tk_max = max_tokens * topk
         self.cap = self.world * self.tk_max
         lib = _lib.load()
@@ -310,7 +315,10 @@ class P2PExpertParallelMoE:
         if self.ffn:
             self.aq = torch.empty((self.cap, self.I), dtype=torch.int8, device=dev)
             self.as_ = torch.empty((self.cap,), dtype=torch.float32, device=dev)
-            self.y = torch.empty((self.cap, H), dtype=torch.bfloat16, device=dev)
+            if not fused_return:
+                self.y = torch.empty((self.cap, H), dtype=torch.bfloat16, device=dev)
+        if fused_return:
+            self.row_addr = torch.empty((self.cap,), dtype=torch.int64, device=dev)   # uint64 addresses
         self.out = torch.empty((max_tokens, self.width), dtype=torch.bfloat16, device=dev)
         self._last_gemm_launches = 0
 
@@ -373,17 +381,26 @@ class P2PExpertParallelMoE:
                                         self.home_pos.data_ptr(), st), "ep_dispatch")
         _lib.check(lib.w4a8_ep_barrier(peers, self.flags_off, self.world, self.rank, self._next_epoch(), st),
                    "ep_barrier")
-        ev.stop()
         # rows this rank serves are counted on the device; the kernels' choice
         # assumes the average, R (every rank routes R slots)
         rows_hint = min(R, self.cap)
         total = self.local_off.data_ptr() + 4 * self.epr
+        if self.fused_return:
+            _lib.check(lib.w4a8_ep_row_addresses(self.src.data_ptr(), total, self.cap, self.width, self.tk_max, peers,
+                                                 self.yhome_off, self.row_addr.data_ptr(), st), "ep_row_addresses")
+        ev.stop()
         w = self.w13
         ev.start("gemm_gate_up")
-        _lib.check(lib.w4a8_group_gemm_moe_hint(self.xq.data_ptr(), H, self.xs.data_ptr(), w.packed.data_ptr(),
-                                                w.scale.data_ptr(), w.zero.data_ptr(), self.local_off.data_ptr(),
-                                                self.h.data_ptr(), self.n13, 1, self.cap, self.epr, self.n13, H,
-                                                self.gs, rows_hint, st), "w4a8_group_gemm_moe")
+        if self.fused_return and not self.ffn:
+            _lib.check(lib.w4a8_group_gemm_moe_rows(self.xq.data_ptr(), H, self.xs.data_ptr(), w.packed.data_ptr(),
+                                                    w.scale.data_ptr(), w.zero.data_ptr(), self.local_off.data_ptr(),
+                                                    self.row_addr.data_ptr(), self.cap, self.epr, self.n13, H,
+                                                    self.gs, rows_hint, st), "w4a8_group_gemm_moe_rows")
+        else:
+            _lib.check(lib.w4a8_group_gemm_moe_hint(self.xq.data_ptr(), H, self.xs.data_ptr(), w.packed.data_ptr(),
+                                                    w.scale.data_ptr(), w.zero.data_ptr(), self.local_off.data_ptr(),
+                                                    self.h.data_ptr(), self.n13, 1, self.cap, self.epr, self.n13, H,
+                                                    self.gs, rows_hint, st), "w4a8_group_gemm_moe")
         ev.stop()
         res = self.h
         if self.ffn:
@@ -394,16 +411,24 @@ class P2PExpertParallelMoE:
             ev.stop()
             w = self.w2
             ev.start("gemm_down")
-            _lib.check(lib.w4a8_group_gemm_moe_hint(self.aq.data_ptr(), self.I, self.as_.data_ptr(),
-                                                    w.packed.data_ptr(), w.scale.data_ptr(), w.zero.data_ptr(),
-                                                    self.local_off.data_ptr(), self.y.data_ptr(), H, 1, self.cap,
-                                                    self.epr, H, self.I, self.gs, rows_hint, st),
-                       "w4a8_group_gemm_moe")
+            if self.fused_return:
+                _lib.check(lib.w4a8_group_gemm_moe_rows(self.aq.data_ptr(), self.I, self.as_.data_ptr(),
+                                                        w.packed.data_ptr(), w.scale.data_ptr(), w.zero.data_ptr(),
+                                                        self.local_off.data_ptr(), self.row_addr.data_ptr(), self.cap,
+                                                        self.epr, H, self.I, self.gs, rows_hint, st),
+                           "w4a8_group_gemm_moe_rows")
+            else:
+                _lib.check(lib.w4a8_group_gemm_moe_hint(self.aq.data_ptr(), self.I, self.as_.data_ptr(),
+                                                        w.packed.data_ptr(), w.scale.data_ptr(), w.zero.data_ptr(),
+                                                        self.local_off.data_ptr(), self.y.data_ptr(), H, 1, self.cap,
+                                                        self.epr, H, self.I, self.gs, rows_hint, st),
+                           "w4a8_group_gemm_moe")
+                res = self.y
             ev.stop()
-            res = self.y
         ev.start("a2a_combine")
-        _lib.check(lib.w4a8_ep_return(res.data_ptr(), res.stride(0), self.width, self.src.data_ptr(), total, rows_hint,
-                                      self.tk_max, peers, self.yhome_off, st), "ep_return")
+        if not self.fused_return:
+            _lib.check(lib.w4a8_ep_return(res.data_ptr(), res.stride(0), self.width, self.src.data_ptr(), total,
+                                          rows_hint, self.tk_max, peers, self.yhome_off, st), "ep_return")
         _lib.check(lib.w4a8_ep_barrier(peers, self.flags_off, self.world, self.rank, self._next_epoch(), st),
                    "ep_barrier")
         ev.stop()

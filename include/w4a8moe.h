@@ -116,6 +116,20 @@ int w4a8_group_gemm_moe_combine(const int8_t* x_q, int64_t x_stride0, const floa
                                 int64_t N, int64_t K, int64_t group_size, int32_t kernel, void* stream);
 
 /*
+ * w4a8_group_gemm_moe_hint with the bf16 rows stored through a row-address
+ * table instead of a strided output (no reference counterpart): row m's N
+ * results go to the contiguous bf16 elements at address out_rows[m] (0: the
+ * row is not stored).  The addresses may lie in another GPU's memory mapped
+ * into this one (NVLink peer memory), so a grouped GEMM can return expert
+ * results straight to the ranks that own the tokens.
+ *   out_rows uint64 [M_total]
+ */
+int w4a8_group_gemm_moe_rows(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
+                             const uint8_t* w_q4_packed, const float* w_scale, const int8_t* w_zero,
+                             const int32_t* expert_offsets, const uint64_t* out_rows, int64_t M_total, int64_t E,
+                             int64_t N, int64_t K, int64_t group_size, int64_t rows_hint, void* stream);
+
+/*
  * Finishes a fused combine (no reference counterpart):
  *   out[t, :] = bf16(acc[t, :]);  acc[t, :] = 0      for t < T
  *   acc fp32 [T, H] (row stride acc_stride0), out bf16 [T, H] (row stride out_stride0)
@@ -267,6 +281,10 @@ int w4a8_moe_align_noalloc(const int32_t* topk_ids, int64_t T, int64_t topk, int
  * w4a8_ep_barrier: every rank signals `epoch` and waits for all.
  * w4a8_ep_return: row r of y (this rank's receive order, r < *total_rows)
  *   into row f of its sender's yhome (src[r] = sender * tk_max + f).
+ * w4a8_ep_row_addresses: the same destinations as a row-address table
+ *   out_rows uint64 [cap_rows] (rows r >= *total_rows get 0), for
+ *   w4a8_group_gemm_moe_rows, whose epilogue then stores the results into
+ *   the senders' yhome directly (no return pass).
  */
 int w4a8_ep_exchange(const int32_t* expert_offsets, int64_t E, int64_t world, int64_t rank,
                      void* const* peers, int64_t counts_off, int64_t flags_off, int32_t epoch,
@@ -281,6 +299,8 @@ int w4a8_ep_barrier(void* const* peers, int64_t flags_off, int64_t world, int64_
 int w4a8_ep_return(const void* y, int64_t y_stride0, int64_t H, const int32_t* src,
                    const int32_t* total_rows, int64_t rows_hint, int64_t tk_max, void* const* peers,
                    int64_t yhome_off, void* stream);
+int w4a8_ep_row_addresses(const int32_t* src, const int32_t* total_rows, int64_t cap_rows, int64_t H,
+                          int64_t tk_max, void* const* peers, int64_t yhome_off, uint64_t* out_rows, void* stream);
 
 /*
  * Health check of the failure-detection path (no reference counterpart; the

@@ -221,3 +221,33 @@ def test_streaming_and_tc_partials_agree_at_decode_size(pkg, cuda, T):
     ref64 = O.group_gemm_f64(*args, gs)
     for name in res:
         assert_gemm_close(res[name][0][m0:m1], ref, ref64, N)
+
+
+@pytest.mark.parametrize("rows_per_expert", [1, 3, 40, 300])   # streaming, mixed, 64- and 256-token tiles
+def test_gemm_row_address_store(pkg, cuda, rows_per_expert):
+    """w4a8_group_gemm_moe_rows stores each row through a table of addresses:
+    rows sent to a permutation of another buffer's rows (0 = not stored) hold
+    exactly the bits the strided store writes."""
+    E, N, K = 8, 512, 1024
+    M = E * rows_per_expert
+    g = pkg.workloads.make_generator(M)
+    x, xs, w, ws, wz, off = pkg.workloads.make_gemm_inputs(E, M, N, K, 128, seed=M)
+    x, xs, w, ws, wz, off = (t.to(cuda) for t in (x, xs, w, ws, wz, off))
+    ref = torch.zeros((M, N), dtype=torch.bfloat16, device=cuda)
+    pkg.w4a8_group_gemm_moe(x, xs, w, ws, wz, off, ref, 128)
+    perm = torch.randperm(M, generator=g).to(cuda)
+    dst = torch.full((M, N), -1.0, dtype=torch.bfloat16, device=cuda)
+    addr = dst.data_ptr() + perm.to(torch.int64) * (N * 2)
+    skip = torch.arange(M, device=cuda) % 7 == 3
+    addr[skip] = 0
+    lib = pkg._lib.load()
+    rc = lib.w4a8_group_gemm_moe_rows(x.data_ptr(), K, xs.data_ptr(), w.data_ptr(), ws.data_ptr(), wz.data_ptr(),
+                                      off.data_ptr(), addr.data_ptr(), M, E, N, K, 128, 0,
+                                      torch.cuda.current_stream().cuda_stream)
+    pkg._lib.check(rc, "w4a8_group_gemm_moe_rows")
+    torch.cuda.synchronize()
+    got = dst[perm]
+    keep = ~skip & (torch.arange(M, device=cuda) < int(off[-1]))
+    assert torch.equal(got[keep].view(torch.int16), ref[keep].view(torch.int16))
+    assert bool((got[skip].float() == -1.0).all())
+    assert pkg.device_status() == 0
