@@ -233,14 +233,16 @@ class P2PExpertParallelMoE:
     it.  Per forward, on every rank: align by global expert, exchange the
     per-expert row counts, dispatch, barrier, gate/up GEMM -> SiLU-mul
     requant -> down GEMM on the receive buffer, return, barrier, combine.
-    With ``fused_return`` (default) the last GEMM's epilogue stores every
-    result row straight into its sender's slot buffer over NVLink (a
-    row-address table built on the device after the dispatch), so the
-    return overlaps the GEMM instead of following it as a separate pass.
+    With ``fused_return`` the last GEMM's epilogue stores every result row
+    straight into its sender's slot buffer over NVLink (a row-address table
+    built on the device after the dispatch) instead of a separate return
+    pass.  Off by default: the epilogue's 2-byte stores per lane (64 bytes per
+    warp store) made the down GEMM 2.5 ms slower at 2 GPUs, more than the
+    1.4 ms return pass (16-byte stores) they replace.
     """
 
     def __init__(self, w13_local: W4A8Weights, w2_local: W4A8Weights | None, num_experts: int, group_size: int,
-                 topk: int, max_tokens: int, group=None, fused_return: bool = True):
+                 topk: int, max_tokens: int, group=None, fused_return: bool = False):
         import torch.distributed._symmetric_memory as symm_mem
         from . import _lib
         self.group = group if group is not None else dist.group.WORLD
