@@ -255,14 +255,19 @@ int w4a8_group_gemm_moe_hint(const int8_t* x_q, int64_t x_stride0, const float* 
 
 int w4a8_group_gemm_moe_rows(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
                              const uint8_t* w_q4_packed, const float* w_scale, const int8_t* w_zero,
-                             const int32_t* expert_offsets, const uint64_t* out_rows, int64_t M_total, int64_t E,
-                             int64_t N, int64_t K, int64_t group_size, int64_t rows_hint, void* stream) {
+                             const int32_t* expert_offsets, void* out_stage, const uint64_t* out_rows,
+                             int64_t M_total, int64_t E, int64_t N, int64_t K, int64_t group_size, int64_t rows_hint,
+                             void* stream) {
   if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
   GemmArgs a{};
   int rc = gemm_setup(&a, x_q, x_stride0, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, M_total, E, N, K,
-                      group_size, W4A8_KERNEL_AUTO, false, nullptr);
+                      group_size, W4A8_KERNEL_AUTO, true, out_stage);
   if (rc != W4A8_OK || M_total == 0) return rc;
   if (out_rows == nullptr) return fail(W4A8_ERR_INVALID, "null row-address table");
+  if ((reinterpret_cast<uintptr_t>(out_stage) & 15) || (N % 8) != 0)
+    return fail(W4A8_ERR_INVALID, "row-address store needs a 16-byte aligned staging output and N %% 8 == 0");
+  a.out_stride0 = N;
+  a.out_stride1 = 1;
   if (rows_hint < 0 || rows_hint > M_total)
     return fail(W4A8_ERR_INVALID, "rows_hint %lld outside [0, M_total=%lld]", (long long)rows_hint, (long long)M_total);
   a.out_rows = out_rows;

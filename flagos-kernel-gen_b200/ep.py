@@ -236,9 +236,9 @@ class P2PExpertParallelMoE:
     With ``fused_return`` the last GEMM's epilogue stores every result row
     straight into its sender's slot buffer over NVLink (a row-address table
     built on the device after the dispatch) instead of a separate return
-    pass.  Off by default: the epilogue's 2-byte stores per lane (64 bytes per
-    warp store) made the down GEMM 2.5 ms slower at 2 GPUs, more than the
-    1.4 ms return pass (16-byte stores) they replace.
+    pass.  Off by default: at 2 GPUs the copies made the down GEMM 1.5 ms
+    slower (its epilogue already sets its pace), about what the 1.6 ms return
+    pass costs.
     """
 
     def __init__(self, w13_local: W4A8Weights, w2_local: W4A8Weights | None, num_experts: int, group_size: int,
@@ -317,8 +317,7 @@ class P2PExpertParallelMoE:
         if self.ffn:
             self.aq = torch.empty((self.cap, self.I), dtype=torch.int8, device=dev)
             self.as_ = torch.empty((self.cap,), dtype=torch.float32, device=dev)
-            if not fused_return:
-                self.y = torch.empty((self.cap, H), dtype=torch.bfloat16, device=dev)
+            self.y = torch.empty((self.cap, H), dtype=torch.bfloat16, device=dev)
         if fused_return:
             self.row_addr = torch.empty((self.cap,), dtype=torch.int64, device=dev)   # uint64 addresses
         self.out = torch.empty((max_tokens, self.width), dtype=torch.bfloat16, device=dev)
@@ -396,8 +395,8 @@ class P2PExpertParallelMoE:
         if self.fused_return and not self.ffn:
             _lib.check(lib.w4a8_group_gemm_moe_rows(self.xq.data_ptr(), H, self.xs.data_ptr(), w.packed.data_ptr(),
                                                     w.scale.data_ptr(), w.zero.data_ptr(), self.local_off.data_ptr(),
-                                                    self.row_addr.data_ptr(), self.cap, self.epr, self.n13, H,
-                                                    self.gs, rows_hint, st), "w4a8_group_gemm_moe_rows")
+                                                    self.h.data_ptr(), self.row_addr.data_ptr(), self.cap, self.epr,
+                                                    self.n13, H, self.gs, rows_hint, st), "w4a8_group_gemm_moe_rows")
         else:
             _lib.check(lib.w4a8_group_gemm_moe_hint(self.xq.data_ptr(), H, self.xs.data_ptr(), w.packed.data_ptr(),
                                                     w.scale.data_ptr(), w.zero.data_ptr(), self.local_off.data_ptr(),
@@ -416,8 +415,9 @@ class P2PExpertParallelMoE:
             if self.fused_return:
                 _lib.check(lib.w4a8_group_gemm_moe_rows(self.aq.data_ptr(), self.I, self.as_.data_ptr(),
                                                         w.packed.data_ptr(), w.scale.data_ptr(), w.zero.data_ptr(),
-                                                        self.local_off.data_ptr(), self.row_addr.data_ptr(), self.cap,
-                                                        self.epr, H, self.I, self.gs, rows_hint, st),
+                                                        self.local_off.data_ptr(), self.y.data_ptr(),
+                                                        self.row_addr.data_ptr(), self.cap, self.epr, H, self.I,
+                                                        self.gs, rows_hint, st),
                            "w4a8_group_gemm_moe_rows")
             else:
                 _lib.check(lib.w4a8_group_gemm_moe_hint(self.aq.data_ptr(), self.I, self.as_.data_ptr(),
@@ -445,11 +445,11 @@ class P2PExpertParallelMoE:
     __call__ = forward
 
     @classmethod
-    def with_synthetic_weights(cls, cfg, T, rank, world, dev, gen):
+    def with_synthetic_weights(cls, cfg, T, rank, world, dev, gen, fused_return: bool = False):
         from . import workloads as W
         epr = cfg.experts // world
         n13 = 2 * cfg.inter if cfg.ffn else cfg.inter
         w13 = W4A8Weights(*W.make_int4_weights(epr, n13, cfg.hidden, cfg.group_size, gen, dev))
         w2 = W4A8Weights(*W.make_int4_weights(epr, cfg.hidden, cfg.inter, cfg.group_size, gen, dev)) \
             if cfg.ffn else None
-        return cls(w13, w2, cfg.experts, cfg.group_size, cfg.topk, T)
+        return cls(w13, w2, cfg.experts, cfg.group_size, cfg.topk, T, fused_return=fused_return)

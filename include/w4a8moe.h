@@ -116,18 +116,22 @@ int w4a8_group_gemm_moe_combine(const int8_t* x_q, int64_t x_stride0, const floa
                                 int64_t N, int64_t K, int64_t group_size, int32_t kernel, void* stream);
 
 /*
- * w4a8_group_gemm_moe_hint with the bf16 rows stored through a row-address
- * table instead of a strided output (no reference counterpart): row m's N
- * results go to the contiguous bf16 elements at address out_rows[m] (0: the
- * row is not stored).  The addresses may lie in another GPU's memory mapped
- * into this one (NVLink peer memory), so a grouped GEMM can return expert
- * results straight to the ranks that own the tokens.
- *   out_rows uint64 [M_total]
+ * w4a8_group_gemm_moe_hint with the bf16 rows also stored through a
+ * row-address table (no reference counterpart): row m's N results go to the
+ * contiguous bf16 elements at address out_rows[m] (0: the row is not
+ * stored).  The addresses may lie in another GPU's memory mapped into this
+ * one (NVLink peer memory), so a grouped GEMM can return expert results
+ * straight to the ranks that own the tokens.  The tensor-core kernel writes
+ * each tile's rows to out_stage first and copies them on in 16-byte pieces;
+ * out_stage's contents afterwards are unspecified.
+ *   out_stage bf16 [M_total, N] contiguous, 16-byte aligned; N % 8 == 0
+ *   out_rows  uint64 [M_total]
  */
 int w4a8_group_gemm_moe_rows(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
                              const uint8_t* w_q4_packed, const float* w_scale, const int8_t* w_zero,
-                             const int32_t* expert_offsets, const uint64_t* out_rows, int64_t M_total, int64_t E,
-                             int64_t N, int64_t K, int64_t group_size, int64_t rows_hint, void* stream);
+                             const int32_t* expert_offsets, void* out_stage, const uint64_t* out_rows,
+                             int64_t M_total, int64_t E, int64_t N, int64_t K, int64_t group_size, int64_t rows_hint,
+                             void* stream);
 
 /*
  * Finishes a fused combine (no reference counterpart):

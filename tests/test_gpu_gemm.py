@@ -225,8 +225,9 @@ def test_streaming_and_tc_partials_agree_at_decode_size(pkg, cuda, T):
 
 @pytest.mark.parametrize("rows_per_expert", [1, 3, 40, 300])   # streaming, mixed, 64- and 256-token tiles
 def test_gemm_row_address_store(pkg, cuda, rows_per_expert):
-    """w4a8_group_gemm_moe_rows stores each row through a table of addresses:
-    rows sent to a permutation of another buffer's rows (0 = not stored) hold
+    """w4a8_group_gemm_moe_rows stores each row through a table of addresses
+    (the tensor-core kernel via its staging output and 16-byte copies): rows
+    sent to a permutation of another buffer's rows (0 = not stored) hold
     exactly the bits the strided store writes."""
     E, N, K = 8, 512, 1024
     M = E * rows_per_expert
@@ -240,9 +241,10 @@ def test_gemm_row_address_store(pkg, cuda, rows_per_expert):
     addr = dst.data_ptr() + perm.to(torch.int64) * (N * 2)
     skip = torch.arange(M, device=cuda) % 7 == 3
     addr[skip] = 0
+    stage = torch.empty((M, N), dtype=torch.bfloat16, device=cuda)
     lib = pkg._lib.load()
     rc = lib.w4a8_group_gemm_moe_rows(x.data_ptr(), K, xs.data_ptr(), w.data_ptr(), ws.data_ptr(), wz.data_ptr(),
-                                      off.data_ptr(), addr.data_ptr(), M, E, N, K, 128, 0,
+                                      off.data_ptr(), stage.data_ptr(), addr.data_ptr(), M, E, N, K, 128, 0,
                                       torch.cuda.current_stream().cuda_stream)
     pkg._lib.check(rc, "w4a8_group_gemm_moe_rows")
     torch.cuda.synchronize()
