@@ -260,7 +260,7 @@ def build_layer(pkg, cfg, T, rank, world, dev, transport="p2p"):
     if transport == "nccl":
         return ep.ExpertParallelMoE.with_synthetic_weights(cfg, T, rank, world, dev, gen)
     return ep.P2PExpertParallelMoE.with_synthetic_weights(cfg, T, rank, world, dev, gen,
-                                                           fused_return=(transport == "p2p_fused_return"))
+                                                           fused_return=(transport == "p2p"))
 
 
 def kernel_bench(pkg, spec: str, steps: int, warmup: int, kernel: int):
@@ -531,7 +531,7 @@ def main():
                     help="skip the parity check, the target points and the routing variant")
     ap.add_argument("--cpu-budget", type=float, default=6.0, help="seconds of CPU work per baseline step")
     ap.add_argument("--kernel", type=int, default=0, help="kernel-only mode: 0 auto, 1 tensor core, 2 CUDA core")
-    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "p2p_fused_return", "nccl"],
+    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "p2p_return_pass", "nccl"],
                     help="expert-parallel transport for N > 1: peer-memory kernels (default) or NCCL all-to-all")
     args = ap.parse_args()
     if args.workload.startswith("gemm_"):

@@ -34,6 +34,7 @@ enum DeviceStatus : int {
   kDevTimeoutAEmpty = 104,
   kDevTimeoutTmemFull = 105,
   kDevTimeoutTmemEmpty = 106,
+  kDevTimeoutTileDone = 107,   // the epilogue never reported a tile's rows (row-address store)
   kDevBadShape = 110,
   kDevTimeoutSelfTest = 120,
   kDevTimeoutPeer = 130,     // a peer rank's signal did not arrive (expert-parallel exchange / barrier)

@@ -115,7 +115,7 @@ struct TcConfig {
   static constexpr int kEpilogueRegs = ER;         // setmaxnreg of the epilogue warpgroups
   static constexpr size_t kSmemTiles =
       size_t(kSeedBytes) + size_t(S) * kXBytes + size_t(S) * kABytes + size_t(kWStages) * kWBytes;
-  static constexpr int kNumBars = 3 * S + 2 * kWStages + 2 * NB + 2;   // + 2 abort-drain barriers
+  static constexpr int kNumBars = 3 * S + 2 * kWStages + 2 * NB + 2 + 2;   // + 2 abort-drain, 2 tile-done barriers
   static constexpr size_t smem_bytes(int E) {
     return 1024 /*alignment slack*/ + kSmemTiles + kNumBars * 8 + 16 + sizeof(int) * 3 * (E + 1);
   }
@@ -209,6 +209,29 @@ __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
   return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
 }
 
+// Row-address store: copies a finished tile's bf16 rows from the staging
+// output to their destination addresses (possibly another GPU's memory),
+// 16 threads per row with 16 bytes each (the weight block's 128 channels),
+// nthreads / 16 rows at a time.  (Batching several rows per thread, out of
+// line, measured slower: 6.19 against 5.96 ms for the 2-GPU down GEMM.)
+__device__ __forceinline__ void copy_tile_rows(const uint64_t* __restrict__ out_rows, const __nv_bfloat16* out,
+                                               int64_t out_stride0, int N, int m0, int rows, int nb, int tid,
+                                               int nthreads) {
+  const int n0 = nb * kBW + (tid & 15) * 8;
+  if (n0 >= N) return;
+  for (int rr = tid >> 4; rr < rows; rr += nthreads >> 4) {
+    const int m = m0 + rr;
+    const uint64_t dst = __ldg(out_rows + m);
+    if (dst == 0) continue;
+    const __nv_bfloat16* src = out + static_cast<int64_t>(m) * out_stride0;
+    __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(dst);
+    if (n0 + 8 <= N)
+      *reinterpret_cast<uint4*>(d + n0) = __ldcg(reinterpret_cast<const uint4*>(src + n0));
+    else
+      for (int c = n0; c < N; ++c) d[c] = __ldcg(src + c);
+  }
+}
+
 template <class C, int kMode>
 __global__ void __launch_bounds__(C::kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_xt,
@@ -233,7 +256,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   uint64_t* tmem_full = a_full + kStages;
   uint64_t* tmem_empty = tmem_full + kBufs;
   uint64_t* drain_bar = tmem_empty + kBufs;   // [2]: one per MMA issuer, used only after an abort
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 2);
+  uint64_t* tile_done = drain_bar + 2;        // [2]: a tile's rows are in the staging output (row-address mode)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_done + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* sched_mem = reinterpret_cast<int*>(tmem_slot + 4);
 
@@ -257,6 +281,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     }
     mbar_init(&drain_bar[0], 1);
     mbar_init(&drain_bar[1], 1);
+    mbar_init(&tile_done[0], C::kEpiWarps);
+    mbar_init(&tile_done[1], C::kEpiWarps);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -425,6 +451,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     const bool zvec = (G % 8) == 0 && (reinterpret_cast<uintptr_t>(a.w_zero) % 8) == 0;
     int stage = 0, astage = 0;
     uint32_t phase = 0, aphase = 0;
+    // Row-address mode: this warpgroup, which has slack beside the epilogue,
+    // streams each finished tile's rows to their destinations one tile
+    // later, so those (peer) stores overlap the next tiles' MMAs.
+    const int copy_tid = threadIdx.x - kTransformWarp0 * 32;
+    Tile prev{};
+    int ti = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const Tile tile = sched_tile(sch, t);
       const int n = tile.nb * kBW + r;
@@ -504,6 +536,24 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         }
         if (++astage == kStages) { astage = 0; aphase ^= 1; }
       }
+      if constexpr (kMode == kModeRows) {
+        if (ti > 0) {
+          if (!mbar_wait(&tile_done[(ti - 1) & 1], ((ti - 1) >> 1) & 1, a.status, kDevTimeoutTileDone, abort_flag))
+            goto tr_done;
+          copy_tile_rows(a.out_rows, a.out, a.out_stride0, a.N, prev.m0, prev.rows, prev.nb, copy_tid,
+                         128 * kTransformWGs);
+        }
+        prev = tile;
+        ++ti;
+      }
+    }
+    if constexpr (kMode == kModeRows) {
+      if (ti > 0) {
+        if (!mbar_wait(&tile_done[(ti - 1) & 1], ((ti - 1) >> 1) & 1, a.status, kDevTimeoutTileDone, abort_flag))
+          goto tr_done;
+        copy_tile_rows(a.out_rows, a.out, a.out_stride0, a.N, prev.m0, prev.rows, prev.nb, copy_tid,
+                       128 * kTransformWGs);
+      }
     }
   tr_done:;
   } else {
@@ -514,7 +564,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     const int r = quarter * 32 + lane;                // weight row within the tile
     const uint64_t magic2 = f2_pack(kMagic, kMagic);
     constexpr int kChunks = kEpiCols / 32;
-    int buf = 0;
+    int buf = 0, tile_i = 0;   // tile_i: this CTA's tiles so far (row-address mode)
     uint32_t bphase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const Tile tile = sched_tile(sch, t);
@@ -614,27 +664,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         }
       }
       if constexpr (kMode == kModeRows) {
-        // Row-address store: the bf16 rows just written to the (contiguous)
-        // staging output are copied to their destinations with 16-byte
-        // stores, each warp its own 32 channels of each token row (4 lanes
-        // per row, 8 rows per instruction).  A 2-byte store per lane and
-        // column, straight to the destination, cost the 2-GPU down GEMM
-        // 4.6 -> 7.1 ms when the destinations were peer memory.
+        // the tile's rows are in the staging output: the transform warpgroup
+        // copies them on (release: the stores above before the arrive)
         __syncwarp();
-        const int rows_wg = min(tile.rows - wg * kEpiCols, kEpiCols);
-        const int n_seg = tile.nb * kBW + quarter * 32 + (lane & 3) * 8;   // 8 channels per lane
-        for (int rr = lane >> 2; rr < rows_wg; rr += 8) {
-          const int m = tile.m0 + wg * kEpiCols + rr;
-          const uint64_t dst = __ldg(a.out_rows + m);
-          if (dst == 0) continue;
-          const __nv_bfloat16* src = a.out + static_cast<int64_t>(m) * a.out_stride0;
-          __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(dst);
-          if (n_seg + 8 <= a.N) {
-            *reinterpret_cast<uint4*>(d + n_seg) = __ldcg(reinterpret_cast<const uint4*>(src + n_seg));
-          } else {
-            for (int c = n_seg; c < a.N; ++c) d[c] = __ldcg(src + c);
-          }
-        }
+        if (lane == 0) mbar_arrive(&tile_done[tile_i & 1]);
+        ++tile_i;
       }
     }
   epi_done:;

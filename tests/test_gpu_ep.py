@@ -50,7 +50,7 @@ def _worker(rank, world, port, q, zipf, transport):
         mine = toks[rank]
         if transport.startswith("p2p"):
             layer = ep.P2PExpertParallelMoE(w13, w2, cfg.experts, cfg.group_size, cfg.topk, max_tokens=256,
-                                            fused_return=(transport == "p2p_fused_return"))
+                                            fused_return=(transport == "p2p"))
         else:
             layer = ep.ExpertParallelMoE(w13, w2, cfg.experts, cfg.group_size, cfg.topk)
         out = layer(mine.x.to(dev), mine.topk_ids.to(dev), mine.topk_weights.to(dev)).clone()
@@ -75,7 +75,7 @@ def _worker(rank, world, port, q, zipf, transport):
         q.put((rank, "error", traceback.format_exc()[-600:]))
 
 
-@pytest.mark.parametrize("transport", ["p2p", "p2p_fused_return", "nccl"])
+@pytest.mark.parametrize("transport", ["p2p", "p2p_return_pass", "nccl"])
 @pytest.mark.parametrize("zipf", [0.0, 1.2])
 def test_ep_two_gpus_matches_single_gpu(zipf, transport):
     if torch.cuda.device_count() < 2:
