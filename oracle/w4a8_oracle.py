@@ -179,8 +179,8 @@ def silu_mul_requant(h_bf16: torch.Tensor):
 # ----------------------------------------------------------------------------- router
 def route_topk(logits, topk: int, scoring: str, renormalize: bool = True):
     """Routing of the benchmark inputs (softmax or sigmoid of fp32 logits [T, E]
-    -> top-k -> weights / their sum; SURVEY's router row N5, the reference takes
-    routing as given).  Ranking: descending logit, ties to the lower expert
+    -> top-k -> weights / their sum; the reference takes routing as given,
+    docs/Task1.md:13).  Ranking: descending logit, ties to the lower expert
     index (the scores are increasing functions of the logits, so this is their
     top-k order).  Scores are fp32; returns (ids int32 [T, k], weights fp32 [T, k])."""
     lg = np.asarray(_np(logits), dtype=np.float32)
