@@ -509,15 +509,29 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
                            static_cast<int64_t>(tile.e) * a.N + n0 + rr};
           if (a.gs == 128) {
             switch (tile.rows) {   // warp-uniform: the tile's token count
-              case 1: gv_row<1, 128, 2, false, kMode>(a, job, tt, G, lane, true); break;
-              case 2: gv_row<2, 128, 2, false, kMode>(a, job, tt, G, lane, true); break;
+              // two groups in flight per lane only when every lane has a second
+              // group (G > 32); with G <= 32 the second slot would repeat the first
+              case 1:
+                if (G > 32) gv_row<1, 128, 2, false, kMode>(a, job, tt, G, lane, true);
+                else gv_row<1, 128, 1, false, kMode>(a, job, tt, G, lane, true);
+                break;
+              case 2:
+                if (G > 32) gv_row<2, 128, 2, false, kMode>(a, job, tt, G, lane, true);
+                else gv_row<2, 128, 1, false, kMode>(a, job, tt, G, lane, true);
+                break;
               case 3: gv_row<3, 128, 1, false, kMode>(a, job, tt, G, lane, true); break;
               default: gv_row<4, 128, 1, false, kMode>(a, job, tt, G, lane, true); break;
             }
           } else {
             switch (tile.rows) {
-              case 1: gv_row<1, 64, 2, false, kMode>(a, job, tt, G, lane, true); break;
-              case 2: gv_row<2, 64, 2, false, kMode>(a, job, tt, G, lane, true); break;
+              case 1:
+                if (G > 32) gv_row<1, 64, 2, false, kMode>(a, job, tt, G, lane, true);
+                else gv_row<1, 64, 1, false, kMode>(a, job, tt, G, lane, true);
+                break;
+              case 2:
+                if (G > 32) gv_row<2, 64, 2, false, kMode>(a, job, tt, G, lane, true);
+                else gv_row<2, 64, 1, false, kMode>(a, job, tt, G, lane, true);
+                break;
               case 3: gv_row<3, 64, 1, false, kMode>(a, job, tt, G, lane, true); break;
               default: gv_row<4, 64, 1, false, kMode>(a, job, tt, G, lane, true); break;
             }
