@@ -128,3 +128,26 @@ def test_router_ties_go_to_the_lower_index(O):
     ids, w = O.route_topk(logits, 4, "sigmoid")
     np.testing.assert_array_equal(ids, [[1, 2, 5, 4]])
     assert abs(float(w.sum()) - 1.0) < 1e-6
+
+
+@pytest.mark.parametrize("fault", ["dropped_group", "scale_1pct", "swapped_rows"])
+def test_layer_tolerance_rejects_planted_errors(pkg, O, fault):
+    """The layer tolerance of the GPU tests (mean|out - ref| <= 1e-3 mean|ref|)
+    rejects the errors it is meant to catch: a layer computed by the oracle
+    with one K-group missing, every weight scale 1 % off, or two tokens'
+    results swapped differs from the true layer by well over the bound."""
+    cfg = pkg.workloads.CONFIGS["small"]
+    inp = pkg.workloads.make_moe_inputs(cfg, 64, seed=3)
+    ref = O.moe_layer(inp.x, inp.topk_ids, inp.topk_weights, inp.w13, None, cfg.group_size).float()
+    packed, scale, zero = inp.w13
+    if fault == "dropped_group":
+        scale = scale.clone()
+        scale[:, :, 3] = 0
+    elif fault == "scale_1pct":
+        scale = scale * 1.01
+    bad = O.moe_layer(inp.x, inp.topk_ids, inp.topk_weights, (packed, scale, zero), None, cfg.group_size).float()
+    if fault == "swapped_rows":
+        bad = bad.clone()
+        bad[[5, 9]] = bad[[9, 5]]
+    rel = (bad - ref).abs().mean().item() / ref.abs().mean().item()
+    assert rel > 5e-3, f"{fault}: relative mean error {rel:.3g} would pass a 1e-3 bound"
