@@ -247,7 +247,7 @@ def cpu_full_step(cfg, T, seed=0):
 
 
 # ----------------------------------------------------------------------------- GPU leg
-def build_layer(pkg, cfg, T, rank, world, dev, transport="p2p", fused_combine=False):
+def build_layer(pkg, cfg, T, rank, world, dev, transport="p2p", fused_combine=False, prepack=False):
     W = pkg.workloads
     gen = W.make_generator(1000 + rank, dev)
     if world == 1:
@@ -255,7 +255,7 @@ def build_layer(pkg, cfg, T, rank, world, dev, transport="p2p", fused_combine=Fa
         w13 = pkg.W4A8Weights(*W.make_int4_weights(cfg.experts, n13, cfg.hidden, cfg.group_size, gen, dev))
         w2 = pkg.W4A8Weights(*W.make_int4_weights(cfg.experts, cfg.hidden, cfg.inter, cfg.group_size, gen, dev)) \
             if cfg.ffn else None
-        return pkg.MoELayer(w13, w2, cfg.group_size, cfg.topk, T, fused_combine=fused_combine)
+        return pkg.MoELayer(w13, w2, cfg.group_size, cfg.topk, T, fused_combine=fused_combine, prepack=prepack)
     ep = importlib.import_module(PKG_NAME + ".ep")
     if transport == "nccl":
         return ep.ExpertParallelMoE.with_synthetic_weights(cfg, T, rank, world, dev, gen)
@@ -531,6 +531,8 @@ def main():
                     help="skip the parity check, the target points and the routing variant")
     ap.add_argument("--cpu-budget", type=float, default=6.0, help="seconds of CPU work per baseline step")
     ap.add_argument("--kernel", type=int, default=0, help="kernel-only mode: 0 auto, 1 tensor core, 2 CUDA core")
+    ap.add_argument("--prepack", action="store_true",
+                    help="single GPU: the layer's weights in the prepacked nibble layout (w4a8_prepack_weights)")
     ap.add_argument("--fused-combine", action="store_true",
                     help="single GPU: top-k combine fused into the down GEMM's epilogue (fp32 atomics)")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "p2p_return_pass", "nccl"],
@@ -549,6 +551,8 @@ def main():
               "routing": f"{cfg.scoring}" + (f"+zipf{cfg.zipf}" if cfg.zipf else " uniform"),
               "parallelism": f"ep{world} ({args.ep_transport})" if world > 1 else "single", "l2": "inputs larger than L2 "
               "(expert weights are GBs; no flush needed)"}
+    if args.prepack and world == 1:
+        config["weights"] = "prepacked nibble layout"
     if args.fused_combine and world == 1:
         config["combine"] = "fused into the down GEMM epilogue (fp32 atomics)"
 
@@ -589,7 +593,7 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     W = pkg.workloads
-    layer = build_layer(pkg, cfg, T, rank, world, dev, args.ep_transport, args.fused_combine)
+    layer = build_layer(pkg, cfg, T, rank, world, dev, args.ep_transport, args.fused_combine, args.prepack)
     inp = W.make_moe_inputs(cfg, T, seed=7 + rank, device=dev, weights=False)
     x, ids, tw = inp.x, inp.topk_ids, inp.topk_weights
 

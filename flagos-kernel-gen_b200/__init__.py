@@ -18,6 +18,7 @@ from .ops import (  # noqa: F401
     gather_rows,
     moe_align,
     moe_combine,
+    prepack_weights,
     quant_scatter,
     router_topk,
     silu_mul_requant,
@@ -31,7 +32,7 @@ from . import ops, workloads  # noqa: F401
 
 __all__ = [
     "w4a8_group_gemm_moe", "w4a8_group_gemm_moe_ex", "w4a8_group_gemm_moe_combine", "combine_finish", "act_quant", "moe_align", "quant_scatter",
-    "router_topk", "silu_mul_requant", "moe_combine", "gather_rows", "device_status", "MoELayer", "HostPipeline", "W4A8Weights",
+    "router_topk", "prepack_weights", "silu_mul_requant", "moe_combine", "gather_rows", "device_status", "MoELayer", "HostPipeline", "W4A8Weights",
     "w4a8_moe",
     "KERNEL_AUTO", "KERNEL_TC", "KERNEL_SIMT", "KERNEL_GEMV", "ops", "workloads",
 ]

@@ -21,6 +21,7 @@ LIB_PATH = os.path.join(LIB_DIR, "libw4a8moe.so")
 
 SOURCES = [
     "capi.cu",
+    "prepack.cu",
     "act_quant.cu",
     "moe_align.cu",
     "ffn_glue.cu",

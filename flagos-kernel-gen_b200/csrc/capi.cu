@@ -235,6 +235,23 @@ int w4a8_group_gemm_moe_ex(const int8_t* x_q, int64_t x_stride0, const float* x_
   return gemm_dispatch(a, kernel, stream);
 }
 
+int w4a8_group_gemm_moe_prepacked(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
+                                  const uint8_t* w_prepacked, const float* w_scale, const int8_t* w_zero,
+                                  const int32_t* expert_offsets, void* out, int64_t out_stride0,
+                                  int64_t out_stride1, int64_t M_total, int64_t E, int64_t N, int64_t K,
+                                  int64_t group_size, int32_t kernel, int32_t* partials, void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return cuda_fail(be, "stream device");
+  GemmArgs a{};
+  int rc = gemm_setup(&a, x_q, x_stride0, x_scale, w_prepacked, w_scale, w_zero, expert_offsets, M_total, E, N, K,
+                      group_size, kernel, true, out);
+  if (rc != W4A8_OK || M_total == 0) return rc;
+  a.partials = partials;
+  a.out_stride0 = out_stride0;
+  a.out_stride1 = out_stride1;
+  a.layout = 1;
+  return gemm_dispatch(a, kernel, stream);
+}
+
 int w4a8_group_gemm_moe_hint(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
                              const uint8_t* w_q4_packed, const float* w_scale, const int8_t* w_zero,
                              const int32_t* expert_offsets, void* out, int64_t out_stride0, int64_t out_stride1,

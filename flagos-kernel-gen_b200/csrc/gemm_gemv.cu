@@ -297,9 +297,12 @@ __device__ __forceinline__ void stage_tokens(const GemmArgs& a, int m0, int rows
       const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
       uint32_t e[4], o[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {   // 8 bytes x0..x7 -> (x0, x2, x4, x6) and (x1, x3, x5, x7)
-        e[q] = __byte_perm(wv[2 * q], wv[2 * q + 1], 0x6420);
-        o[q] = __byte_perm(wv[2 * q], wv[2 * q + 1], 0x7531);
+      for (int q = 0; q < 4; ++q) {
+        // reference layout: 8 bytes x0..x7 -> (x0, x2, x4, x6) and (x1, x3, x5, x7);
+        // prepacked weights: (x0, x1, x2, x3) and (x4, x5, x6, x7), the k order of
+        // a weight word's low and high nibbles
+        e[q] = a.layout == 0 ? __byte_perm(wv[2 * q], wv[2 * q + 1], 0x6420) : wv[2 * q];
+        o[q] = a.layout == 0 ? __byte_perm(wv[2 * q], wv[2 * q + 1], 0x7531) : wv[2 * q + 1];
         s = __dp4a(static_cast<int>(wv[2 * q]), 0x01010101, s);
         s = __dp4a(static_cast<int>(wv[2 * q + 1]), 0x01010101, s);
       }

@@ -75,8 +75,10 @@ gemm_simt_kernel(GemmArgs a) {
           lo = static_cast<int8_t>(static_cast<int16_t>(p & 0x0F) - z);
           hi = static_cast<int8_t>(static_cast<int16_t>(p >> 4) - z);
         }
-        s_w[r * wstride + 2 * b] = lo;
-        s_w[r * wstride + 2 * b + 1] = hi;
+        // byte b holds k = 2b, 2b+1 (reference) or 8(b/4) + b%4, + 4 (prepacked)
+        const int pl = a.layout == 0 ? 2 * b : 8 * (b >> 2) + (b & 3);
+        s_w[r * wstride + pl] = lo;
+        s_w[r * wstride + pl + (a.layout == 0 ? 1 : 4)] = hi;
       }
       __syncthreads();
       if (n < a.N) {

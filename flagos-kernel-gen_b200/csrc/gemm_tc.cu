@@ -517,12 +517,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
           const uint32_t c8 = (cb & 0x80u) * 0x01010101u;
           const uint32_t wv[4] = {pk[c].x, pk[c].y, pk[c].z, pk[c].w};
           uint32_t o[8];
+          if (a.layout == 0) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t lo = wv[q] & 0x0F0F0F0Fu;
-            const uint32_t hi = (wv[q] >> 4) & 0x0F0F0F0Fu;
-            o[2 * q] = pack_fold(__byte_perm(lo, hi, 0x5140), c7, c8);
-            o[2 * q + 1] = pack_fold(__byte_perm(lo, hi, 0x7362), c7, c8);
+            for (int q = 0; q < 4; ++q) {
+              const uint32_t lo = wv[q] & 0x0F0F0F0Fu;          // k = 8q + 0, 2, 4, 6
+              const uint32_t hi = (wv[q] >> 4) & 0x0F0F0F0Fu;   // k = 8q + 1, 3, 5, 7
+              o[2 * q] = pack_fold(__byte_perm(lo, hi, 0x5140), c7, c8);
+              o[2 * q + 1] = pack_fold(__byte_perm(lo, hi, 0x7362), c7, c8);
+            }
+          } else {   // prepacked: the low nibbles are k = 8q..8q+3, the high ones 8q+4..8q+7
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              o[2 * q] = pack_fold(wv[q] & 0x0F0F0F0Fu, c7, c8);
+              o[2 * q + 1] = pack_fold((wv[q] >> 4) & 0x0F0F0F0Fu, c7, c8);
+            }
           }
           const int j0 = 2 * c, j1 = 2 * c + 1;
           *reinterpret_cast<uint4*>(dst_row + ((j0 ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);

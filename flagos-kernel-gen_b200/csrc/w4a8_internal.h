@@ -42,6 +42,10 @@ struct GemmArgs {
   // N contiguous elements at address out_rows[m] (0: row not stored) — e.g.
   // straight into another GPU's buffer over NVLink peer memory.
   const uint64_t* out_rows = nullptr;
+  // Weight nibble layout: 0 = the reference's (byte j of a row holds k = 2j
+  // low, 2j + 1 high); 1 = the word-interleaved prepack of w4a8_prepack_weights
+  // (byte b of 32-bit word q holds k = 8q + b low, 8q + 4 + b high).
+  int layout = 0;
 };
 
 #ifdef __CUDACC__

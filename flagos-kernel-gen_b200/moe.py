@@ -65,13 +65,24 @@ class MoELayer:
     """Routed W4A8 MoE (gate/up -> SiLU-mul -> down, or a single up GEMM)."""
 
     def __init__(self, w13: W4A8Weights, w2: W4A8Weights | None, group_size: int, topk: int,
-                 max_tokens: int, align_block: int = 128, fused_combine: bool = False):
+                 max_tokens: int, align_block: int = 128, fused_combine: bool = False,
+                 prepack: bool = False):
         """``fused_combine``: the last grouped GEMM adds its weighted rows into
         an fp32 token accumulator in its epilogue (``w4a8_group_gemm_moe_combine``)
         instead of writing [R, H] bf16 rows for a separate combine; the fp32
         additions then run in no fixed order (results may differ from the
-        unfused, j-ascending combine in the last fp32 bit)."""
+        unfused, j-ascending combine in the last fp32 bit).
+        ``prepack``: the layer keeps a copy of the weights in the prepacked
+        nibble layout (``ops.prepack_weights``) and runs its GEMMs on it
+        (same results)."""
+        if prepack and fused_combine:
+            raise ValueError("prepack and fused_combine are not combined")
         self.fused_combine = fused_combine
+        self.prepacked = prepack
+        if prepack:
+            w13 = W4A8Weights(ops.prepack_weights(w13.packed), w13.scale, w13.zero)
+            if w2 is not None:
+                w2 = W4A8Weights(ops.prepack_weights(w2.packed), w2.scale, w2.zero)
         self.w13, self.w2 = w13, w2
         self.gs, self.topk = group_size, topk
         E, N13, H = w13.shape
@@ -161,8 +172,8 @@ class MoELayer:
             ops.w4a8_group_gemm_moe_combine(xq, xs, self.w13.packed, self.w13.scale, self.w13.zero, self.offsets,
                                             self.sorted_ids, tw, self.acc, self.gs)
         else:
-            ops.w4a8_group_gemm_moe(xq, xs, self.w13.packed, self.w13.scale, self.w13.zero, self.offsets, h,
-                                    self.gs)
+            ops.w4a8_group_gemm_moe_ex(xq, xs, self.w13.packed, self.w13.scale, self.w13.zero, self.offsets, h,
+                                       self.gs, prepacked=self.prepacked)
         ev.stop()
         y = h
         if self.ffn:
@@ -176,8 +187,8 @@ class MoELayer:
                                                 self.sorted_ids, tw, self.acc, self.gs)
             else:
                 y = self.y[:R]
-                ops.w4a8_group_gemm_moe(aq, as_, self.w2.packed, self.w2.scale, self.w2.zero, self.offsets, y,
-                                        self.gs)
+                ops.w4a8_group_gemm_moe_ex(aq, as_, self.w2.packed, self.w2.scale, self.w2.zero, self.offsets, y,
+                                           self.gs, prepacked=self.prepacked)
             ev.stop()
         ev.start("combine")
         if fuse:

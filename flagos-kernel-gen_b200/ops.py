@@ -113,11 +113,13 @@ def w4a8_group_gemm_moe(
 
 
 def w4a8_group_gemm_moe_ex(x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, out, group_size,
-                           kernel: int = _lib.KERNEL_AUTO, partials: torch.Tensor | None = None):
+                           kernel: int = _lib.KERNEL_AUTO, partials: torch.Tensor | None = None,
+                           prepacked: bool = False):
     """``w4a8_group_gemm_moe`` with a kernel selector and the optional int32
     per-group partial-sum export ``partials`` (int32 [M_total, N, K/group_size],
     the layout of the reference's einsum; the library writes it group-major,
-    [G, M_total, N], and it is transposed into ``partials`` here)."""
+    [G, M_total, N], and it is transposed into ``partials`` here).
+    ``prepacked``: ``w_q4_packed`` is in the layout of ``prepack_weights``."""
     dev, x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, M_total, E, N, K = _gemm_operands(
         x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_offsets, out, group_size)
     staging = None
@@ -127,13 +129,33 @@ def w4a8_group_gemm_moe_ex(x_q, x_scale, w_q4_packed, w_scale, w_zero, expert_of
             raise ValueError(f"partials must be a contiguous int32 tensor of shape {(M_total, N, G)}")
         staging = torch.zeros((G, M_total, N), dtype=torch.int32, device=dev)
     lib = _lib.load()
-    rc = lib.w4a8_group_gemm_moe_ex(
+    fn = lib.w4a8_group_gemm_moe_prepacked if prepacked else lib.w4a8_group_gemm_moe_ex
+    rc = fn(
         x_q.data_ptr(), x_q.stride(0) if M_total > 0 else K, x_scale.data_ptr(), w_q4_packed.data_ptr(),
         w_scale.data_ptr(), w_zero.data_ptr(), expert_offsets.data_ptr(), out.data_ptr(), out.stride(0),
         out.stride(1), M_total, E, N, K, group_size, kernel, _ptr(staging), _stream(dev))
     _lib.check(rc, "w4a8_group_gemm_moe")
     if staging is not None:
         partials.copy_(staging.permute(1, 2, 0))
+    return out
+
+
+def prepack_weights(w_q4_packed: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Offline prepack of packed int4 weights (uint8 [..., K/2], contiguous):
+    the same nibbles in the word-interleaved layout the grouped GEMMs read
+    without byte permutes (``prepacked=True``).  ``out`` may be the input
+    (in place)."""
+    dev = _require_cuda(w_q4_packed)
+    if w_q4_packed.dtype != torch.uint8 or not w_q4_packed.is_contiguous():
+        raise TypeError("w_q4_packed must be a contiguous uint8 tensor")
+    if out is None:
+        out = torch.empty_like(w_q4_packed)
+    if out.shape != w_q4_packed.shape or out.dtype != torch.uint8 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous uint8 tensor of the input's shape")
+    K = w_q4_packed.shape[-1] * 2
+    rows = w_q4_packed.numel() // max(w_q4_packed.shape[-1], 1)
+    rc = _lib.load().w4a8_prepack_weights(w_q4_packed.data_ptr(), out.data_ptr(), rows, K, _stream(dev))
+    _lib.check(rc, "prepack_weights")
     return out
 
 

@@ -96,6 +96,29 @@ int w4a8_group_gemm_moe_hint(const int8_t* x_q, int64_t x_stride0, const float* 
                              int64_t group_size, int64_t rows_hint, void* stream);
 
 /*
+ * Offline weight prepack (no reference counterpart; the reference unpacks the
+ * packed bytes on every call, docs/Task1.md:78-81).  Writes the same int4
+ * weights in the word-interleaved nibble layout: for each 32-bit word q of a
+ * row (k = 8q .. 8q + 7), byte b (0..3) holds k = 8q + b in its low nibble
+ * and k = 8q + 4 + b in its high nibble (the reference layout has k = 2j and
+ * 2j + 1 in byte j).  Same size; scales and zero points are unchanged.  With
+ * this layout the int4 -> int8 unpack needs no byte permutes.  out may equal
+ * w_q4_packed (in place).
+ *   w_q4_packed, out  uint8 [rows, K/2] contiguous, 16-byte aligned; K % 64 == 0
+ */
+int w4a8_prepack_weights(const uint8_t* w_q4_packed, uint8_t* out, int64_t rows, int64_t K, void* stream);
+
+/*
+ * w4a8_group_gemm_moe_ex on weights prepacked by w4a8_prepack_weights (all
+ * kernels; results identical to the reference layout's).
+ */
+int w4a8_group_gemm_moe_prepacked(const int8_t* x_q, int64_t x_stride0, const float* x_scale,
+                                  const uint8_t* w_prepacked, const float* w_scale, const int8_t* w_zero,
+                                  const int32_t* expert_offsets, void* out, int64_t out_stride0,
+                                  int64_t out_stride1, int64_t M_total, int64_t E, int64_t N, int64_t K,
+                                  int64_t group_size, int32_t kernel, int32_t* partials, void* stream);
+
+/*
  * Grouped W4A8 GEMM with the weighted top-k combine fused into its epilogue.
  * Replaces the bf16 store of docs/Task1.md:110-112 (the reference's operator
  * ends there) followed by a separate combine: each row m's result is still

@@ -45,6 +45,22 @@ def unpack_int4(packed) -> np.ndarray:
     return out
 
 
+def prepack(packed) -> np.ndarray:
+    """The word-interleaved prepack layout of ``w4a8_prepack_weights``: in
+    each 32-bit word q of a row (k = 8q .. 8q + 7), byte b holds k = 8q + b
+    in its low nibble and k = 8q + 4 + b in its high nibble."""
+    nib = unpack_int4(packed).astype(np.uint8)                  # [..., K]
+    w = nib.reshape(nib.shape[:-1] + (-1, 2, 4))                # [..., K/8, half, b]
+    return (w[..., 0, :] | (w[..., 1, :] << 4)).reshape(nib.shape[:-1] + (-1,)).astype(np.uint8)
+
+
+def unpack_prepacked(packed) -> np.ndarray:
+    """uint8 [..., K/2] in the prepack layout -> nibbles int16 [..., K] in k order."""
+    p = _np(packed).astype(np.uint8).reshape(_np(packed).shape[:-1] + (-1, 4))
+    lo, hi = p & 0x0F, (p >> 4) & 0x0F
+    return np.concatenate([lo, hi], axis=-1).reshape(p.shape[:-2] + (-1,)).astype(np.int16)
+
+
 def fold_zero(w_int4: np.ndarray, w_zero, group_size: int) -> np.ndarray:
     """int8(nibble - zero) with the per-group zero broadcast over K; the int16
     difference wraps on the cast exactly like ``.to(torch.int8)``

@@ -151,3 +151,15 @@ def test_layer_tolerance_rejects_planted_errors(pkg, O, fault):
         bad[[5, 9]] = bad[[9, 5]]
     rel = (bad - ref).abs().mean().item() / ref.abs().mean().item()
     assert rel > 5e-3, f"{fault}: relative mean error {rel:.3g} would pass a 1e-3 bound"
+
+
+def test_prepack_layout_round_trip(O):
+    """The prepack layout holds the same nibbles: unpacking it gives the
+    reference layout's nibbles in k order, and it differs from the input
+    (so a kernel reading it with the wrong layout would be caught)."""
+    rng = np.random.default_rng(5)
+    packed = rng.integers(0, 256, size=(3, 7, 64), dtype=np.uint8)
+    pp = O.prepack(packed)
+    assert pp.shape == packed.shape and pp.dtype == np.uint8
+    np.testing.assert_array_equal(O.unpack_prepacked(pp), O.unpack_int4(packed))
+    assert not np.array_equal(pp, packed)
