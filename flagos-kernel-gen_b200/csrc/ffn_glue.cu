@@ -100,6 +100,66 @@ silu_mul_requant_vec_kernel(const __nv_bfloat16* __restrict__ h, int64_t h_strid
   }
 }
 
+// One warp per row for I <= 32 * 8 * kWVec (Qwen3's I = 768): each lane owns
+// kV 16-byte vectors of gate and up, the row maximum is a warp reduction, and
+// a CTA of 8 warps serves 8 rows.  The arithmetic is that of the
+// CTA-per-row kernel, element by element (the same bits).  Measured on B200:
+// 32768 rows x 768 in 66 us against 132 us for a CTA per row; at I = 2048
+// the lane's 64 values need more registers than two CTAs per SM leave
+// (665 us, spilling, against 605 us), so wider rows keep a CTA per row.
+constexpr int kWVec = 4;
+template <int kV>
+__global__ void __launch_bounds__(kGThreads, 2)
+silu_mul_requant_warp_kernel(const __nv_bfloat16* __restrict__ h, int64_t h_stride0, int I, int R,
+                             int8_t* __restrict__ q, int64_t q_stride0, float* __restrict__ s_out,
+                             const int32_t* __restrict__ valid_rows) {
+  const int lane = threadIdx.x & 31;
+  const int64_t lim = valid_rows != nullptr ? *valid_rows : R;
+  const int nv = I / 8;
+  for (int64_t row = blockIdx.x * static_cast<int64_t>(kGThreads / 32) + (threadIdx.x >> 5); row < lim;
+       row += static_cast<int64_t>(gridDim.x) * (kGThreads / 32)) {
+    const __nv_bfloat16* hr = h + row * h_stride0;
+    uint4 gv[kV], uv[kV];
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+      const int v = lane + 32 * i;
+      if (v < nv) {
+        gv[i] = __ldg(reinterpret_cast<const uint4*>(hr) + v);
+        uv[i] = __ldg(reinterpret_cast<const uint4*>(hr + I) + v);
+      }
+    }
+    float y[kV][8];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+      if (lane + 32 * i < nv) {
+        const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv[i]);
+        const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uv[i]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 g = __bfloat1622float2(g2[j]);
+          const float2 u = __bfloat1622float2(u2[j]);
+          y[i][2 * j] = silu_mul(g.x, u.x);
+          y[i][2 * j + 1] = silu_mul(g.y, u.y);
+          amax = fmaxf(amax, fmaxf(fabsf(y[i][2 * j]), fabsf(y[i][2 * j + 1])));
+        }
+      }
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
+    const float s = fmaxf(__fdiv_rn(amax, 127.f), 1e-10f);
+    if (lane == 0) s_out[row] = s;
+    int8_t* qr = q + row * q_stride0;
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+      const int v = lane + 32 * i;
+      if (v < nv)
+        reinterpret_cast<uint2*>(qr)[v] = make_uint2(quant4(y[i][0], y[i][1], y[i][2], y[i][3], s),
+                                                     quant4(y[i][4], y[i][5], y[i][6], y[i][7], s));
+    }
+  }
+}
+
 // One CTA per row.  The fp32 products are staged in shared memory (I <= 16384).
 __global__ void __launch_bounds__(kGThreads)
 silu_mul_requant_kernel(const __nv_bfloat16* __restrict__ h, int64_t h_stride0, int I,
@@ -259,6 +319,24 @@ cudaError_t launch_silu_mul_requant(const __nv_bfloat16* h, int64_t h_stride0, i
                                     int64_t q_stride0, float* s, const int32_t* valid_rows,
                                     cudaStream_t stream) {
   if (R <= 0) return cudaSuccess;
+  const bool wvec = (I % 8) == 0 && I / 8 <= 32 * kWVec && (h_stride0 % 8) == 0 &&
+                    (reinterpret_cast<uintptr_t>(h) % 16) == 0 && (q_stride0 % 8) == 0 &&
+                    (reinterpret_cast<uintptr_t>(q) % 8) == 0;
+  if (wvec) {   // one warp per row, 8 rows per CTA; with valid_rows a resident grid strides over them
+    int grid = (R + kGThreads / 32 - 1) / (kGThreads / 32);
+    if (valid_rows != nullptr) {
+      int dev = 0, sms = 0;
+      cudaGetDevice(&dev);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      grid = grid < sms * 8 ? grid : sms * 8;
+    }
+    const int kv = (I / 8 + 31) / 32;
+    if (kv <= 2)
+      silu_mul_requant_warp_kernel<2><<<grid, kGThreads, 0, stream>>>(h, h_stride0, I, R, q, q_stride0, s, valid_rows);
+    else
+      silu_mul_requant_warp_kernel<4><<<grid, kGThreads, 0, stream>>>(h, h_stride0, I, R, q, q_stride0, s, valid_rows);
+    return cudaGetLastError();
+  }
   if (valid_rows != nullptr) {   // rows counted on the device: a resident grid strides over them
     int dev = 0, sms = 0;
     cudaGetDevice(&dev);
