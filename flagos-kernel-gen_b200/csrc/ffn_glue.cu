@@ -206,6 +206,53 @@ silu_mul_requant_kernel(const __nv_bfloat16* __restrict__ h, int64_t h_stride0, 
 // One CTA per (token, column slice); each thread owns 8 consecutive columns
 // (16-byte vectors).  The column slices (gridDim.y) give a decode-sized batch
 // enough CTAs to fill the GPU.
+// Vector path with the token's kK slots unrolled: all kK 16-byte loads are in
+// flight before the first add (a loop over a run-time top-k issued them one
+// after another, each after the previous one's adds), and the adds still run
+// j ascending with every product and sum rounded to fp32 (the same bits).
+template <int kK>
+__global__ void __launch_bounds__(kGThreads)
+moe_combine_unrolled_kernel(const __nv_bfloat16* __restrict__ y, int64_t y_stride0, const int32_t* __restrict__ inv_pos,
+                            const float* __restrict__ topk_w, int H, __nv_bfloat16* __restrict__ out,
+                            int64_t out_stride0) {
+  const int t = blockIdx.x;
+  const int32_t* pos = inv_pos + static_cast<int64_t>(t) * kK;
+  const float* wt = topk_w + static_cast<int64_t>(t) * kK;
+  __nv_bfloat16* o = out + static_cast<int64_t>(t) * out_stride0;
+  int p[kK];
+  float w[kK];
+#pragma unroll
+  for (int j = 0; j < kK; ++j) {
+    p[j] = __ldg(pos + j);
+    w[j] = __ldg(wt + j);
+  }
+  for (int c = blockIdx.y * kGThreads + threadIdx.x; c < H / 8; c += kGThreads * gridDim.y) {
+    uint4 v[kK];
+#pragma unroll
+    for (int j = 0; j < kK; ++j)
+      if (p[j] >= 0) v[j] = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(p[j]) * y_stride0) + c);
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kK; ++j) {
+      if (p[j] < 0) continue;
+      const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&v[j]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(v2[i]);
+        acc[2 * i] = __fadd_rn(acc[2 * i], __fmul_rn(w[j], f.x));
+        acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __fmul_rn(w[j], f.y));
+      }
+    }
+    uint4 r;
+    __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r2[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+    reinterpret_cast<uint4*>(o)[c] = r;
+  }
+}
+
 __global__ void __launch_bounds__(kGThreads)
 moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int64_t y_stride0, const int32_t* __restrict__ inv_pos,
                    const float* __restrict__ topk_w, int topk, int H, __nv_bfloat16* __restrict__ out,
@@ -365,8 +412,18 @@ cudaError_t launch_moe_combine(const __nv_bfloat16* y, int64_t y_stride0, const 
                                int64_t out_stride0, cudaStream_t stream) {
   if (T <= 0) return cudaSuccess;
   const int slices = std::max(1, std::min(8, (H / 8 + kGThreads - 1) / kGThreads));   // column slices per token
-  moe_combine_kernel<<<dim3(T, slices), kGThreads, 0, stream>>>(y, y_stride0, inv_pos, topk_w, topk, H, out,
-                                                                 out_stride0);
+  const bool vec = (H & 7) == 0 && (y_stride0 & 7) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out) & 15) == 0 && (out_stride0 & 7) == 0;
+  const dim3 grid(T, slices);
+  if (vec && topk == 8) {
+    moe_combine_unrolled_kernel<8><<<grid, kGThreads, 0, stream>>>(y, y_stride0, inv_pos, topk_w, H, out, out_stride0);
+  } else if (vec && topk == 2) {
+    moe_combine_unrolled_kernel<2><<<grid, kGThreads, 0, stream>>>(y, y_stride0, inv_pos, topk_w, H, out, out_stride0);
+  } else if (vec && topk == 4) {
+    moe_combine_unrolled_kernel<4><<<grid, kGThreads, 0, stream>>>(y, y_stride0, inv_pos, topk_w, H, out, out_stride0);
+  } else {
+    moe_combine_kernel<<<grid, kGThreads, 0, stream>>>(y, y_stride0, inv_pos, topk_w, topk, H, out, out_stride0);
+  }
   return cudaGetLastError();
 }
 
