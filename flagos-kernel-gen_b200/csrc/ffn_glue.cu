@@ -203,9 +203,6 @@ silu_mul_requant_kernel(const __nv_bfloat16* __restrict__ h, int64_t h_stride0, 
   }
 }
 
-// One CTA per (token, column slice); each thread owns 8 consecutive columns
-// (16-byte vectors).  The column slices (gridDim.y) give a decode-sized batch
-// enough CTAs to fill the GPU.
 // Vector path with the token's kK slots unrolled: all kK 16-byte loads are in
 // flight before the first add (a loop over a run-time top-k issued them one
 // after another, each after the previous one's adds), and the adds still run
@@ -253,6 +250,9 @@ moe_combine_unrolled_kernel(const __nv_bfloat16* __restrict__ y, int64_t y_strid
   }
 }
 
+// One CTA per (token, column slice); each thread owns 8 consecutive columns
+// (16-byte vectors).  The column slices (gridDim.y) give a decode-sized batch
+// enough CTAs to fill the GPU.
 __global__ void __launch_bounds__(kGThreads)
 moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int64_t y_stride0, const int32_t* __restrict__ inv_pos,
                    const float* __restrict__ topk_w, int topk, int H, __nv_bfloat16* __restrict__ out,
