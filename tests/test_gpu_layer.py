@@ -245,3 +245,28 @@ def test_layer_fused_combine_against_oracle(pkg, cuda, cfg_name, T):
     width = c.hidden if inp.w2 is not None else c.inter
     for o in outs:
         assert_layer_close(o, ref, width, "fused layer")
+
+
+@pytest.mark.parametrize("I", [512, 768, 2048, 14336])   # one warp per row (<= 1024) and one CTA per row
+def test_silu_requant_rows_counted_on_device(pkg, cuda, I):
+    """w4a8_silu_mul_requant_rows (the expert-parallel receive buffer's form:
+    the row count read on the device) writes exactly the bits of
+    w4a8_silu_mul_requant on its first rows and leaves the rows past the count
+    untouched."""
+    R, valid = 700, 523
+    g = pkg.workloads.make_generator(I)
+    h = (torch.randn((R, 2 * I), generator=g) * 2).to(torch.bfloat16).to(cuda)
+    q_ref = torch.zeros((R, I), dtype=torch.int8, device=cuda)
+    s_ref = torch.zeros((R,), dtype=torch.float32, device=cuda)
+    pkg.silu_mul_requant(h, q_ref, s_ref)
+    q = torch.full((R, I), 77, dtype=torch.int8, device=cuda)
+    s = torch.full((R,), -1.0, dtype=torch.float32, device=cuda)
+    cnt = torch.tensor([valid], dtype=torch.int32, device=cuda)
+    lib = pkg._lib.load()
+    rc = lib.w4a8_silu_mul_requant_rows(h.data_ptr(), 2 * I, R, I, q.data_ptr(), s.data_ptr(), cnt.data_ptr(),
+                                        torch.cuda.current_stream().cuda_stream)
+    pkg._lib.check(rc, "w4a8_silu_mul_requant_rows")
+    torch.cuda.synchronize()
+    assert torch.equal(q[:valid], q_ref[:valid])
+    assert torch.equal(s[:valid].view(torch.int32), s_ref[:valid].view(torch.int32))
+    assert bool((q[valid:] == 77).all()) and bool((s[valid:] == -1.0).all())
