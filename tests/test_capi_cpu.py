@@ -137,3 +137,39 @@ def test_product_path_never_imports_the_oracle():
             if f.endswith((".py", ".cu", ".cuh", ".h")):
                 text = open(os.path.join(root, f), encoding="utf-8").read()
                 assert "import oracle" not in text and "from oracle" not in text, f
+
+
+def test_newer_entry_points_reject_bad_arguments_without_a_gpu(pkg):
+    """Router, prepack, row-address GEMM and return-address entry points check
+    their arguments on the host before any launch."""
+    from importlib import import_module
+    L = import_module("flagos-kernel-gen_b200._lib")
+    lib = L.load()
+    P = 1 << 20   # a stand-in pointer value: every call below fails validation before using it
+
+    def router(**over):
+        a = dict(logits=P, ls0=256, T=16, E=256, topk=8, scoring=1, renorm=1, ids=P, w=P, x=None, xs0=0, H=0,
+                 xq=None, qs0=0, xscale=None, stream=None)
+        a.update(over)
+        return lib.w4a8_router_topk(*a.values())
+    for bad in (dict(topk=0), dict(topk=257, E=256), dict(topk=33, E=64), dict(E=1025, ls0=1025), dict(scoring=2),
+                dict(ls0=100), dict(x=P, H=0), dict(x=P, H=7168, xs0=7168, qs0=7168, xq=None, xscale=P)):
+        assert router(**bad) == L.W4A8_ERR_INVALID, bad
+    assert router(T=0) == L.W4A8_OK
+
+    assert lib.w4a8_prepack_weights(P, P, 4, 100, None) == L.W4A8_ERR_INVALID      # K not a multiple of 64
+    assert lib.w4a8_prepack_weights(P + 8, P, 4, 128, None) == L.W4A8_ERR_INVALID  # unaligned input
+    assert lib.w4a8_prepack_weights(P, P, 0, 128, None) == L.W4A8_OK
+
+    def rows(**over):
+        a = dict(x_q=P, xs0=512, x_scale=P, w=P, ws=P, wz=P, off=P, stage=P, addr=P, M=32, E=4, N=512, K=512,
+                 gs=128, hint=0, stream=None)
+        a.update(over)
+        return lib.w4a8_group_gemm_moe_rows(*a.values())
+    for bad in (dict(addr=None), dict(stage=None), dict(N=500), dict(stage=P + 8), dict(hint=33), dict(gs=96)):
+        assert rows(**bad) == L.W4A8_ERR_INVALID, bad
+    assert rows(M=0) == L.W4A8_OK
+
+    assert lib.w4a8_ep_row_addresses(P, P, 16, 7168, 0, P, 0, P, None) == L.W4A8_ERR_INVALID   # tk_max 0
+    assert lib.w4a8_ep_row_addresses(None, P, 16, 7168, 8, P, 0, P, None) == L.W4A8_ERR_INVALID
+    assert lib.w4a8_ep_row_addresses(P, P, 0, 7168, 8, P, 0, P, None) == L.W4A8_OK
