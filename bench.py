@@ -260,7 +260,8 @@ def build_layer(pkg, cfg, T, rank, world, dev, transport="p2p", fused_combine=Fa
     if transport == "nccl":
         return ep.ExpertParallelMoE.with_synthetic_weights(cfg, T, rank, world, dev, gen)
     return ep.P2PExpertParallelMoE.with_synthetic_weights(cfg, T, rank, world, dev, gen,
-                                                           fused_return=(transport == "p2p"))
+                                                           fused_return=(transport != "p2p_return_pass"),
+                                                           dedup_dispatch=(transport != "p2p_plain_dispatch"))
 
 
 def kernel_bench(pkg, spec: str, steps: int, warmup: int, kernel: int):
@@ -535,7 +536,7 @@ def main():
                     help="single GPU: the layer's weights in the prepacked nibble layout (w4a8_prepack_weights)")
     ap.add_argument("--fused-combine", action="store_true",
                     help="single GPU: top-k combine fused into the down GEMM's epilogue (fp32 atomics)")
-    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "p2p_return_pass", "nccl"],
+    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "p2p_return_pass", "p2p_plain_dispatch", "nccl"],
                     help="expert-parallel transport for N > 1: peer-memory kernels (default) or NCCL all-to-all")
     args = ap.parse_args()
     if args.workload.startswith("gemm_"):

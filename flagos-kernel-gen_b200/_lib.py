@@ -44,6 +44,9 @@ SIGNATURES = {
     "w4a8_ep_exchange": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i32, _i64, _p, _p, _p]),
     "w4a8_ep_dispatch": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p,
                                         _i64, _i64, _i64, _p, _p]),
+    "w4a8_ep_dispatch_dedup": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p,
+                                              _p, _i64, _i64, _i64, _i64, _p, _p]),
+    "w4a8_ep_replicate": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _i64, _p]),
     "w4a8_ep_barrier": (ctypes.c_int, [_p, _i64, _i64, _i64, _i32, _p]),
     "w4a8_prepack_weights": (ctypes.c_int, [_p, _p, _i64, _i64, _p]),
     "w4a8_group_gemm_moe_prepacked": (ctypes.c_int, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,

@@ -169,6 +169,27 @@ __global__ void ep_row_addr_kernel(const int32_t* __restrict__ src, const int32_
   }
 }
 
+// Deduplicated dispatch, receiver side: row r < *total_rows whose dup entry
+// names an earlier row of the same token takes that row's bytes (the sender
+// crossed NVLink once per destination rank, not once per slot).
+__global__ void ep_replicate_kernel(int8_t* __restrict__ xq, int H, const int32_t* __restrict__ dup,
+                                    const int32_t* __restrict__ total_rows) {
+  const int rows = *total_rows;
+  const bool vec = (H % 16) == 0 && (reinterpret_cast<uintptr_t>(xq) % 16) == 0;
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int p = dup[r];
+    if (p < 0) continue;
+    const int8_t* src = xq + static_cast<int64_t>(p) * H;
+    int8_t* dst = xq + static_cast<int64_t>(r) * H;
+    if (vec) {
+      for (int v = threadIdx.x; v < H / 16; v += blockDim.x)
+        reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(src)[v];
+    } else {
+      for (int c = threadIdx.x; c < H; c += blockDim.x) dst[c] = src[c];
+    }
+  }
+}
+
 int ep_fail(int code, const char* msg) {
   set_last_error(msg);
   return code;
@@ -216,6 +237,44 @@ int w4a8_ep_dispatch(const void* x, int64_t x_stride0, int64_t T, int64_t H, con
              dest_base, reinterpret_cast<uint8_t* const*>(peers), xq_off, xs_off, src_off, home_pos};
   const cudaError_t e = launch_ep_dispatch(static_cast<const __nv_bfloat16*>(x), x_stride0, (int)T, (int)H, d,
                                            static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? W4A8_OK : ep_fail(W4A8_ERR_CUDA, cudaGetErrorString(e));
+}
+
+int w4a8_ep_dispatch_dedup(const void* x, int64_t x_stride0, int64_t T, int64_t H, const int32_t* topk_ids,
+                           int64_t topk, int64_t E, int64_t world, int64_t rank, int64_t tk_max,
+                           const int32_t* expert_offsets, const int32_t* inv_pos, const int32_t* dest_base,
+                           void* const* peers, int64_t xq_off, int64_t xs_off, int64_t src_off, int64_t dup_off,
+                           int32_t* home_pos, void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return ep_fail(W4A8_ERR_CUDA, cudaGetErrorString(be));
+  if (T < 0 || H <= 0 || H > 16384 || topk <= 0 || topk > 256 || world < 1 || world > kEpMaxWorld || rank < 0 ||
+      rank >= world || E <= 0 || E % world || T * topk > tk_max || world * tk_max > INT32_MAX || dup_off < 0)
+    return ep_fail(W4A8_ERR_INVALID,
+                   "w4a8_ep_dispatch_dedup: bad sizes (H <= 16384, T*topk <= tk_max, world*tk_max < 2^31, dup_off >= 0)");
+  if (T == 0) return W4A8_OK;
+  if (x == nullptr || topk_ids == nullptr || expert_offsets == nullptr || inv_pos == nullptr || dest_base == nullptr ||
+      peers == nullptr || home_pos == nullptr)
+    return ep_fail(W4A8_ERR_INVALID, "w4a8_ep_dispatch_dedup: null pointer");
+  PeerRows d{topk_ids, (int)topk, (int)E, (int)(E / world), (int)rank, tk_max, (int)H, expert_offsets, inv_pos,
+             dest_base, reinterpret_cast<uint8_t* const*>(peers), xq_off, xs_off, src_off, home_pos, dup_off};
+  const cudaError_t e = launch_ep_dispatch(static_cast<const __nv_bfloat16*>(x), x_stride0, (int)T, (int)H, d,
+                                           static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? W4A8_OK : ep_fail(W4A8_ERR_CUDA, cudaGetErrorString(e));
+}
+
+int w4a8_ep_replicate(void* buf, int64_t xq_off, int64_t dup_off, int64_t H, const int32_t* total_rows,
+                      int64_t rows_hint, void* stream) {
+  if (cudaError_t be = bind_stream_device(stream); be != cudaSuccess) return ep_fail(W4A8_ERR_CUDA, cudaGetErrorString(be));
+  if (H <= 0 || rows_hint < 0 || xq_off < 0 || dup_off < 0) return ep_fail(W4A8_ERR_INVALID, "w4a8_ep_replicate: bad sizes");
+  if (buf == nullptr || total_rows == nullptr) return ep_fail(W4A8_ERR_INVALID, "w4a8_ep_replicate: null pointer");
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = rows_hint > 0 ? rows_hint : 1;
+  const int grid = static_cast<int>(want < sms * 8 ? want : sms * 8);
+  uint8_t* b = static_cast<uint8_t*>(buf);
+  ep_replicate_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<int8_t*>(b + xq_off), (int)H, reinterpret_cast<const int32_t*>(b + dup_off), total_rows);
+  const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? W4A8_OK : ep_fail(W4A8_ERR_CUDA, cudaGetErrorString(e));
 }
 

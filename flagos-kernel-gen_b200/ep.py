@@ -238,11 +238,13 @@ class P2PExpertParallelMoE:
     built on the device after the dispatch; the GEMM's transform warpgroup
     copies each finished tile's rows while later tiles run) instead of a
     separate return pass: 14.56 against 14.72 ms per step at 2 GPUs, 14.25
-    against 15.55 at 8.
+    against 15.55 at 8.  With ``dedup_dispatch`` (default) a token's int8 row
+    crosses to each remote rank once, however many of its experts that rank
+    owns; the owner copies it into the other slots' rows after the barrier.
     """
 
     def __init__(self, w13_local: W4A8Weights, w2_local: W4A8Weights | None, num_experts: int, group_size: int,
-                 topk: int, max_tokens: int, group=None, fused_return: bool = True):
+                 topk: int, max_tokens: int, group=None, fused_return: bool = True, dedup_dispatch: bool = True):
         import torch.distributed._symmetric_memory as symm_mem
         from . import _lib
         self.group = group if group is not None else dist.group.WORLD
@@ -265,6 +267,7 @@ class P2PExpertParallelMoE:
         self.device = dev
         self.max_tokens = max_tokens
         self.fused_return = fused_return
+        self.dedup = dedup_dispatch
         self.tk_max = max_tokens * topk
         self.cap = self.world * self.tk_max
         lib = _lib.load()
@@ -285,6 +288,8 @@ class P2PExpertParallelMoE:
         off += rup(4 * self.cap)
         self.yhome_off = off
         off += rup(2 * self.tk_max * self.width)
+        self.dup_off = off
+        off += rup(4 * self.cap)
         self.buf_bytes = off
         if hasattr(symm_mem, "enable_symm_mem_for_group"):
             try:
@@ -340,8 +345,8 @@ class P2PExpertParallelMoE:
     def launches_per_forward(self, tokens: int | None = None) -> int:
         R = (tokens if tokens is not None else self.max_tokens) * self.topk
         g = len(cuda_ops.gemm_auto_kernels(R, self.epr))
-        # align 3, exchange, dispatch, barrier, GEMMs, (SiLU, GEMMs), return, barrier, combine
-        return 3 + 3 + g + ((1 + g) if self.ffn else 0) + 3
+        # align 3, exchange, dispatch, barrier, (replicate), GEMMs, (SiLU, GEMMs), return, barrier, combine
+        return 3 + 3 + int(self.dedup) + g + ((1 + g) if self.ffn else 0) + 3
 
     def _next_epoch(self) -> int:
         self.epoch += 1
@@ -376,16 +381,26 @@ class P2PExpertParallelMoE:
                                         self.local_off.data_ptr(), st), "ep_exchange")
         ev.stop()
         ev.start("a2a_dispatch")
-        _lib.check(lib.w4a8_ep_dispatch(x.data_ptr(), x.stride(0), T, H, ids.data_ptr(), k, self.E, self.world,
-                                        self.rank, self.tk_max, self.off_g.data_ptr(), self.inv.data_ptr(),
-                                        self.dest_base.data_ptr(), peers, self.xq_off, self.xs_off, self.src_off,
-                                        self.home_pos.data_ptr(), st), "ep_dispatch")
+        if self.dedup:
+            _lib.check(lib.w4a8_ep_dispatch_dedup(x.data_ptr(), x.stride(0), T, H, ids.data_ptr(), k, self.E,
+                                                  self.world, self.rank, self.tk_max, self.off_g.data_ptr(),
+                                                  self.inv.data_ptr(), self.dest_base.data_ptr(), peers, self.xq_off,
+                                                  self.xs_off, self.src_off, self.dup_off, self.home_pos.data_ptr(),
+                                                  st), "ep_dispatch_dedup")
+        else:
+            _lib.check(lib.w4a8_ep_dispatch(x.data_ptr(), x.stride(0), T, H, ids.data_ptr(), k, self.E, self.world,
+                                            self.rank, self.tk_max, self.off_g.data_ptr(), self.inv.data_ptr(),
+                                            self.dest_base.data_ptr(), peers, self.xq_off, self.xs_off, self.src_off,
+                                            self.home_pos.data_ptr(), st), "ep_dispatch")
         _lib.check(lib.w4a8_ep_barrier(peers, self.flags_off, self.world, self.rank, self._next_epoch(), st),
                    "ep_barrier")
         # rows this rank serves are counted on the device; the kernels' choice
         # assumes the average, R (every rank routes R slots)
         rows_hint = min(R, self.cap)
         total = self.local_off.data_ptr() + 4 * self.epr
+        if self.dedup:
+            _lib.check(lib.w4a8_ep_replicate(self.buf.data_ptr(), self.xq_off, self.dup_off, H, total, rows_hint, st),
+                       "ep_replicate")
         if self.fused_return:
             _lib.check(lib.w4a8_ep_row_addresses(self.src.data_ptr(), total, self.cap, self.width, self.tk_max, peers,
                                                  self.yhome_off, self.row_addr.data_ptr(), st), "ep_row_addresses")
@@ -445,11 +460,13 @@ class P2PExpertParallelMoE:
     __call__ = forward
 
     @classmethod
-    def with_synthetic_weights(cls, cfg, T, rank, world, dev, gen, fused_return: bool = True):
+    def with_synthetic_weights(cls, cfg, T, rank, world, dev, gen, fused_return: bool = True,
+                               dedup_dispatch: bool = True):
         from . import workloads as W
         epr = cfg.experts // world
         n13 = 2 * cfg.inter if cfg.ffn else cfg.inter
         w13 = W4A8Weights(*W.make_int4_weights(epr, n13, cfg.hidden, cfg.group_size, gen, dev))
         w2 = W4A8Weights(*W.make_int4_weights(epr, cfg.hidden, cfg.inter, cfg.group_size, gen, dev)) \
             if cfg.ffn else None
-        return cls(w13, w2, cfg.experts, cfg.group_size, cfg.topk, T, fused_return=fused_return)
+        return cls(w13, w2, cfg.experts, cfg.group_size, cfg.topk, T, fused_return=fused_return,
+                   dedup_dispatch=dedup_dispatch)

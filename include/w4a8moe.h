@@ -305,6 +305,14 @@ int w4a8_moe_align_noalloc(const int32_t* topk_ids, int64_t T, int64_t topk, int
  * w4a8_ep_dispatch: quantises each token once (as w4a8_act_quant) and stores
  *   its row, scale and return address into the owners' receive buffers;
  *   home_pos int32 [T*topk] = the slot's index, or -1 for dropped slots.
+ * w4a8_ep_dispatch_dedup: as w4a8_ep_dispatch, but a token's int8 row
+ *   crosses to each remote rank once: a later slot of the same token on the
+ *   same remote rank stores only its scale, return address and, in the dup
+ *   int32 [cap_rows] region at dup_off, the receive row of that first slot
+ *   (-1 for rows whose bytes were sent).  The owner then runs
+ *   w4a8_ep_replicate after the barrier.
+ * w4a8_ep_replicate: on the receiving rank, row r < *total_rows of xq whose
+ *   dup entry is p >= 0 takes the bytes of row p.
  * w4a8_ep_barrier: every rank signals `epoch` and waits for all.
  * w4a8_ep_return: row r of y (this rank's receive order, r < *total_rows)
  *   into row f of its sender's yhome (src[r] = sender * tk_max + f).
@@ -321,6 +329,13 @@ int w4a8_ep_dispatch(const void* x, int64_t x_stride0, int64_t T, int64_t H, con
                      const int32_t* expert_offsets, const int32_t* inv_pos, const int32_t* dest_base,
                      void* const* peers, int64_t xq_off, int64_t xs_off, int64_t src_off,
                      int32_t* home_pos, void* stream);
+int w4a8_ep_dispatch_dedup(const void* x, int64_t x_stride0, int64_t T, int64_t H, const int32_t* topk_ids,
+                           int64_t topk, int64_t E, int64_t world, int64_t rank, int64_t tk_max,
+                           const int32_t* expert_offsets, const int32_t* inv_pos, const int32_t* dest_base,
+                           void* const* peers, int64_t xq_off, int64_t xs_off, int64_t src_off, int64_t dup_off,
+                           int32_t* home_pos, void* stream);
+int w4a8_ep_replicate(void* buf, int64_t xq_off, int64_t dup_off, int64_t H, const int32_t* total_rows,
+                      int64_t rows_hint, void* stream);
 int w4a8_ep_barrier(void* const* peers, int64_t flags_off, int64_t world, int64_t rank, int32_t epoch,
                     void* stream);
 int w4a8_ep_return(const void* y, int64_t y_stride0, int64_t H, const int32_t* src,

@@ -173,3 +173,14 @@ def test_newer_entry_points_reject_bad_arguments_without_a_gpu(pkg):
     assert lib.w4a8_ep_row_addresses(P, P, 16, 7168, 0, P, 0, P, None) == L.W4A8_ERR_INVALID   # tk_max 0
     assert lib.w4a8_ep_row_addresses(None, P, 16, 7168, 8, P, 0, P, None) == L.W4A8_ERR_INVALID
     assert lib.w4a8_ep_row_addresses(P, P, 0, 7168, 8, P, 0, P, None) == L.W4A8_OK
+
+    def dedup(**over):
+        a = dict(x=P, xs0=7168, T=16, H=7168, ids=P, topk=8, E=256, world=2, rank=0, tk_max=128, off=P, inv=P,
+                 base=P, peers=P, xq_off=0, xs_off=0, src_off=0, dup_off=256, home=P, stream=None)
+        a.update(over)
+        return lib.w4a8_ep_dispatch_dedup(*a.values())
+    for bad in (dict(dup_off=-1), dict(tk_max=127), dict(rank=2), dict(E=255), dict(H=0), dict(ids=None)):
+        assert dedup(**bad) == L.W4A8_ERR_INVALID, bad
+    assert dedup(T=0) == L.W4A8_OK
+    assert lib.w4a8_ep_replicate(P, 0, -1, 7168, P, 16, None) == L.W4A8_ERR_INVALID
+    assert lib.w4a8_ep_replicate(P, 0, 256, 7168, None, 16, None) == L.W4A8_ERR_INVALID

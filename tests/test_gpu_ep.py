@@ -1,5 +1,7 @@
 """Expert parallelism on 2 GPUs (skipped with fewer), both transports (the
-peer-memory kernels and NCCL all-to-all): every rank's output equals, bit for
+peer-memory kernels -- with the return streamed by the down GEMM or as its own
+pass, with the deduplicated or the per-slot dispatch -- and NCCL
+all-to-all): every rank's output equals, bit for
 bit, a single-GPU MoELayer run over the tokens of all ranks (same weights),
 and a second forward through the same buffers gives the same bits.  Rows reach an expert in a
 different order under EP, but each row's result does not depend on the other
@@ -50,7 +52,8 @@ def _worker(rank, world, port, q, zipf, transport):
         mine = toks[rank]
         if transport.startswith("p2p"):
             layer = ep.P2PExpertParallelMoE(w13, w2, cfg.experts, cfg.group_size, cfg.topk, max_tokens=256,
-                                            fused_return=(transport == "p2p"))
+                                            fused_return=(transport != "p2p_return_pass"),
+                                            dedup_dispatch=(transport != "p2p_plain_dispatch"))
         else:
             layer = ep.ExpertParallelMoE(w13, w2, cfg.experts, cfg.group_size, cfg.topk)
         out = layer(mine.x.to(dev), mine.topk_ids.to(dev), mine.topk_weights.to(dev)).clone()
@@ -75,7 +78,7 @@ def _worker(rank, world, port, q, zipf, transport):
         q.put((rank, "error", traceback.format_exc()[-600:]))
 
 
-@pytest.mark.parametrize("transport", ["p2p", "p2p_return_pass", "nccl"])
+@pytest.mark.parametrize("transport", ["p2p", "p2p_return_pass", "p2p_plain_dispatch", "nccl"])
 @pytest.mark.parametrize("zipf", [0.0, 1.2])
 def test_ep_two_gpus_matches_single_gpu(zipf, transport):
     if torch.cuda.device_count() < 2:
