@@ -276,6 +276,173 @@ __device__ __forceinline__ void gv_row(const GemmArgs& a, const RowJob& j, const
   }
 }
 
+// Exact int32 partials of one K-group (one lane's) for two weight rows
+// against the same R token rows, zero points that cannot wrap (the sums of
+// partials_nowrap); each token chunk is read from shared memory once for
+// both rows.
+template <int R, int GS>
+__device__ __forceinline__ void partials_nowrap_pair(const uint8_t* const (&wg)[2], const uint8_t* xeg,
+                                                     const uint8_t* xog, int rot, int half_k, int (&p)[2][R],
+                                                     const int (&z)[2], const int (&sxv)[R]) {
+  constexpr int kCpg = GS / 32;
+  int se[2][R], so[2][R];
+#pragma unroll
+  for (int n = 0; n < 2; ++n)
+#pragma unroll
+    for (int r = 0; r < R; ++r) { se[n][r] = -z[n] * sxv[r]; so[n][r] = 0; }
+#pragma unroll
+  for (int i = 0; i < kCpg; ++i) {
+    const int ch = 16 * ((i + rot) & (kCpg - 1));
+    uint32_t lo[2][4], hi[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      const uint4 w = *reinterpret_cast<const uint4*>(wg[n] + ch);
+      lo[n][0] = w.x & 0x0F0F0F0Fu; lo[n][1] = w.y & 0x0F0F0F0Fu;
+      lo[n][2] = w.z & 0x0F0F0F0Fu; lo[n][3] = w.w & 0x0F0F0F0Fu;
+      hi[n][0] = w.x & 0xF0F0F0F0u; hi[n][1] = w.y & 0xF0F0F0F0u;
+      hi[n][2] = w.z & 0xF0F0F0F0u; hi[n][3] = w.w & 0xF0F0F0F0u;
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const uint4 xe = *reinterpret_cast<const uint4*>(xeg + r * half_k + ch);
+      const uint4 xo = *reinterpret_cast<const uint4*>(xog + r * half_k + ch);
+#pragma unroll
+      for (int n = 0; n < 2; ++n) {
+        se[n][r] = dp4a_us(lo[n][0], xe.x, se[n][r]);
+        so[n][r] = dp4a_us(hi[n][0], xo.x, so[n][r]);
+        se[n][r] = dp4a_us(lo[n][1], xe.y, se[n][r]);
+        so[n][r] = dp4a_us(hi[n][1], xo.y, so[n][r]);
+        se[n][r] = dp4a_us(lo[n][2], xe.z, se[n][r]);
+        so[n][r] = dp4a_us(hi[n][2], xo.z, so[n][r]);
+        se[n][r] = dp4a_us(lo[n][3], xe.w, se[n][r]);
+        so[n][r] = dp4a_us(hi[n][3], xo.w, so[n][r]);
+      }
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < 2; ++n)
+#pragma unroll
+    for (int r = 0; r < R; ++r) p[n][r] = se[n][r] + (so[n][r] >> 4);
+}
+
+// Short rows (at most 16 K-groups) at one token row per expert: a half-warp
+// takes two weight rows (j[0], j[1]) and each lane reads its K-group's token
+// chunks once for both, so the shared-memory reads per weight byte fall from
+// three to two (weights, even-k and odd-k token bytes for one row against
+// weights of two rows and one set of token bytes).  Each row's sum is formed
+// as in gv_row (same lane order, same reduction), so the outputs equal
+// gv_row's bit for bit.  write[n] is false for a row the caller has not got
+// (computed on a duplicate index, not stored).
+template <int R, int GS, int kMode>
+__device__ __forceinline__ void gv_pair_half(const GemmArgs& a, const RowJob (&j)[2], const bool (&write)[2],
+                                             const TokenTile& tt, int G, int lane) {
+  constexpr int kRot = GS == 128 ? 1 : 2;
+  const int l = lane & 15;
+  const int half_k = a.K >> 1;
+  const int rot = l >> kRot;
+  float acc[2][R];
+#pragma unroll
+  for (int n = 0; n < 2; ++n)
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[n][r] = 0.f;
+  for (int g = l; g < G; g += 16) {
+    int z[2], sxv[R];
+    const uint8_t* wg[2];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      z[n] = j[n].z != nullptr ? j[n].z[g] : a.w_zero[j[n].grow * G + g];
+      wg[n] = j[n].w + g * (GS / 2);
+    }
+    const uint8_t* xeg = tt.xe + g * (GS / 2);
+    const uint8_t* xog = tt.xo + g * (GS / 2);
+#pragma unroll
+    for (int r = 0; r < R; ++r) sxv[r] = tt.sx[r * G + g];
+    int p[2][R];
+    if (z[0] >= kWrapZero && z[1] >= kWrapZero) {
+      partials_nowrap_pair<R, GS>(wg, xeg, xog, rot, half_k, p, z, sxv);
+    } else {
+#pragma unroll
+      for (int n = 0; n < 2; ++n) {
+        if (z[n] < kWrapZero) {
+          partials_wrap<R, GS>(wg[n], xeg, xog, rot, half_k, z[n], p[n]);
+        } else {
+          const uint8_t* const w1[1] = {wg[n]};
+          const uint8_t* const e1[1] = {xeg};
+          const uint8_t* const o1[1] = {xog};
+          int p1[1][R], z1[1] = {z[n]}, s1[1][R];
+#pragma unroll
+          for (int r = 0; r < R; ++r) s1[0][r] = sxv[r];
+          partials_nowrap<R, GS, 1>(w1, e1, o1, rot, half_k, p1, z1, s1);
+#pragma unroll
+          for (int r = 0; r < R; ++r) p[n][r] = p1[0][r];
+        }
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      const float ws = j[n].ws != nullptr ? j[n].ws[g] : __ldg(a.w_scale + j[n].grow * G + g);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        acc[n][r] = fmaf(static_cast<float>(p[n][r]), ws, acc[n][r]);
+        if constexpr (kMode == kGvPartials)
+          if (write[n]) a.partials[(static_cast<int64_t>(g) * a.M_total + j[n].m0 + r) * a.N + j[n].n] = p[n][r];
+      }
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < 2; ++n) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float v = acc[n][r];
+#pragma unroll
+      for (int d = 8; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+      if (l == 0 && write[n]) {
+        const int m = j[n].m0 + r;
+        if constexpr (kMode == kGvCombine) {
+          store_output(a, m, j[n].n, v);
+        } else if constexpr (kMode == kGvRowAddr) {
+          const uint64_t row = __ldg(a.out_rows + m);
+          if (row != 0) reinterpret_cast<__nv_bfloat16*>(row)[j[n].n] = __float2bfloat16_rn(v * tt.xsc[r]);
+        } else {
+          a.out[static_cast<int64_t>(m) * a.out_stride0 + static_cast<int64_t>(j[n].n) * a.out_stride1] =
+              __float2bfloat16_rn(v * tt.xsc[r]);
+        }
+      }
+    }
+  }
+}
+
+// One ring stage of short rows (at most 16 K-groups; rows [0, rows) of the
+// block at n0) against the tile's R token rows.  R = 1: a pair of weight
+// rows per half-warp, four per warp (gv_pair_half); R >= 2: one row per
+// half-warp, two per warp (the second row's chains would not fit the
+// register budget).
+template <int R, int GS, int kMode>
+__device__ __forceinline__ void gv_short_stage(const GemmArgs& a, const GvParams& gp, const Tile& tile, int n0,
+                                               int rows, const uint8_t* st, const float* s_ws, const int8_t* s_z,
+                                               const TokenTile& tt, int G, int warp, int lane) {
+  auto job = [&](int ri) {
+    return RowJob{st + ri * gp.row_bytes, gp.meta_bulk ? s_z + ri * G : nullptr,
+                  gp.meta_bulk ? s_ws + ri * G : nullptr, tile.m0, n0 + ri,
+                  static_cast<int64_t>(tile.e) * a.N + n0 + ri};
+  };
+  if constexpr (R == 1) {
+    for (int rr = 4 * warp; rr < rows; rr += 4 * kGvConsumers) {
+      const int r0 = rr + 2 * (lane >> 4);
+      const bool write[2] = {r0 < rows, r0 + 1 < rows};
+      const int i0 = write[0] ? r0 : rr;
+      const RowJob jb[2] = {job(i0), job(write[1] ? r0 + 1 : i0)};
+      gv_pair_half<1, GS, kMode>(a, jb, write, tt, G, lane);
+    }
+  } else {
+    for (int rr = 2 * warp; rr < rows; rr += 2 * kGvConsumers) {
+      const int mine = rr + (lane >> 4);
+      const bool write = mine < rows;
+      gv_row<R, GS, 1, true, kMode>(a, job(write ? mine : rr), tt, G, lane, write);
+    }
+  }
+}
+
 // Stages the token rows [m0, m0 + rows) of x_q: per 32-value chunk the 16
 // even-k bytes and the 16 odd-k bytes, and per K-group the sum of its
 // values.  Called by all consumer threads between two consumer barriers.
@@ -481,28 +648,20 @@ gemm_gemv_kernel(const GemmArgs a, const GvParams gp) {
       const float* s_ws = reinterpret_cast<const float*>(st + gp.stage_w);
       const int8_t* s_z = reinterpret_cast<const int8_t*>(st + gp.stage_w + gp.ws_bytes);
       if constexpr (kShort) {
-        // short rows: two per warp, one per half-warp
-        for (int rr = 2 * warp; rr < rows; rr += 2 * kGvConsumers) {
-          const int mine = rr + (lane >> 4);
-          const bool write = mine < rows;
-          const int ri = write ? mine : rr;
-          const RowJob job{st + ri * gp.row_bytes, gp.meta_bulk ? s_z + ri * G : nullptr,
-                           gp.meta_bulk ? s_ws + ri * G : nullptr, tile.m0, n0 + ri,
-                           static_cast<int64_t>(tile.e) * a.N + n0 + ri};
-          if (a.gs == 128) {
-            switch (tile.rows) {   // warp-uniform: the tile's token count
-              case 1: gv_row<1, 128, 1, true, kMode>(a, job, tt, G, lane, write); break;
-              case 2: gv_row<2, 128, 1, true, kMode>(a, job, tt, G, lane, write); break;
-              case 3: gv_row<3, 128, 1, true, kMode>(a, job, tt, G, lane, write); break;
-              default: gv_row<4, 128, 1, true, kMode>(a, job, tt, G, lane, write); break;
-            }
-          } else {
-            switch (tile.rows) {
-              case 1: gv_row<1, 64, 1, true, kMode>(a, job, tt, G, lane, write); break;
-              case 2: gv_row<2, 64, 1, true, kMode>(a, job, tt, G, lane, write); break;
-              case 3: gv_row<3, 64, 1, true, kMode>(a, job, tt, G, lane, write); break;
-              default: gv_row<4, 64, 1, true, kMode>(a, job, tt, G, lane, write); break;
-            }
+        // the token count is switched on once per stage, outside the row loop
+        if (a.gs == 128) {
+          switch (tile.rows) {   // warp-uniform: the tile's token count
+            case 1: gv_short_stage<1, 128, kMode>(a, gp, tile, n0, rows, st, s_ws, s_z, tt, G, warp, lane); break;
+            case 2: gv_short_stage<2, 128, kMode>(a, gp, tile, n0, rows, st, s_ws, s_z, tt, G, warp, lane); break;
+            case 3: gv_short_stage<3, 128, kMode>(a, gp, tile, n0, rows, st, s_ws, s_z, tt, G, warp, lane); break;
+            default: gv_short_stage<4, 128, kMode>(a, gp, tile, n0, rows, st, s_ws, s_z, tt, G, warp, lane); break;
+          }
+        } else {
+          switch (tile.rows) {
+            case 1: gv_short_stage<1, 64, kMode>(a, gp, tile, n0, rows, st, s_ws, s_z, tt, G, warp, lane); break;
+            case 2: gv_short_stage<2, 64, kMode>(a, gp, tile, n0, rows, st, s_ws, s_z, tt, G, warp, lane); break;
+            case 3: gv_short_stage<3, 64, kMode>(a, gp, tile, n0, rows, st, s_ws, s_z, tt, G, warp, lane); break;
+            default: gv_short_stage<4, 64, kMode>(a, gp, tile, n0, rows, st, s_ws, s_z, tt, G, warp, lane); break;
           }
         }
       } else {
