@@ -178,7 +178,7 @@ __global__ void ep_replicate_kernel(int8_t* __restrict__ xq, int H, const int32_
   const bool vec = (H % 16) == 0 && (reinterpret_cast<uintptr_t>(xq) % 16) == 0;
   for (int r = blockIdx.x; r < rows; r += gridDim.x) {
     const int p = dup[r];
-    if (p < 0) continue;
+    if (p < 0 || p >= rows) continue;   // a first row is always one of this forward's rows
     const int8_t* src = xq + static_cast<int64_t>(p) * H;
     int8_t* dst = xq + static_cast<int64_t>(r) * H;
     if (vec) {
