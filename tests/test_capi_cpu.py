@@ -184,3 +184,35 @@ def test_newer_entry_points_reject_bad_arguments_without_a_gpu(pkg):
     assert dedup(T=0) == L.W4A8_OK
     assert lib.w4a8_ep_replicate(P, 0, -1, 7168, P, 16, None) == L.W4A8_ERR_INVALID
     assert lib.w4a8_ep_replicate(P, 0, 256, 7168, None, 16, None) == L.W4A8_ERR_INVALID
+
+
+def _header_declarations():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = re.sub(r"//[^\n]*", "", text)
+    out = {}
+    for name, params in re.findall(r"\b(w4a8_\w+)\s*\(([^;{]*?)\)\s*;", text, flags=re.S):
+        ps = [p.strip() for p in params.split(",") if p.strip()]
+        out[name] = [] if ps == ["void"] else ps
+    return out
+
+
+def test_ctypes_signatures_match_the_header(pkg):
+    """Every entry point's ctypes argument list has the header's arity and,
+    parameter by parameter, the same kind: pointer, 64-bit integer, 32-bit
+    integer, size_t.  A shifted or missing argument would otherwise reach the
+    library as a wrong pointer or stream without any error on the host."""
+    from importlib import import_module
+    L = import_module("flagos-kernel-gen_b200._lib")
+    decls = _header_declarations()
+    assert set(decls) == set(declared_functions())
+    scalar = {"int64_t": ctypes.c_int64, "int32_t": ctypes.c_int32, "int": ctypes.c_int, "size_t": ctypes.c_size_t}
+    for name, params in decls.items():
+        _, argtypes = L.SIGNATURES[name]
+        assert len(argtypes) == len(params), f"{name}: header has {len(params)} parameters, ctypes {len(argtypes)}"
+        for i, (p, t) in enumerate(zip(params, argtypes)):
+            if "*" in p:
+                assert t is ctypes.c_void_p or issubclass(t, ctypes._Pointer), f"{name} arg {i} ({p}) is {t}"
+            else:
+                ctype = re.sub(r"^const\s+", "", p).rsplit(None, 1)[0]
+                assert ctypes.sizeof(t) == ctypes.sizeof(scalar[ctype]), f"{name} arg {i} ({p}) is {t}"
